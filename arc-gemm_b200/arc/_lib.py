@@ -1,0 +1,104 @@
+"""ctypes binding of libarcb200.so (the C ABI declared in include/arc_b200.h).
+
+There is no fallback: if the library is missing or fails to load, every GEMM call
+raises. Building it is `python -m arc.build` (or `__graft_entry__.build()`).
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+from .build import LIB_PATH
+
+ARC_OK = 0
+ARC_ERR_INVALID_ARGUMENT = 1
+ARC_ERR_UNSUPPORTED = 2
+ARC_ERR_CUDA = 3
+ARC_ERR_NO_DEVICE = 4
+ARC_ERR_DEVICE_TIMEOUT = 5
+
+
+class ArcError(RuntimeError):
+    """A nonzero arc_status_t from the native library."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+class Plan(ctypes.Structure):
+    _fields_ = [
+        ("split", ctypes.c_int),
+        ("token_tile", ctypes.c_int),
+        ("weight_rows", ctypes.c_int),
+        ("k_split", ctypes.c_int),
+        ("grid", ctypes.c_int),
+        ("load_stages", ctypes.c_int),
+    ]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+# Every symbol include/arc_b200.h declares, with its ctypes signature.
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+SIGNATURES = {
+    "arc_version": ([], _I),
+    "arc_status_string": ([_I], ctypes.c_char_p),
+    "arc_last_error": ([], ctypes.c_char_p),
+    "arc_matmul_bf16": ([_P, _P, _P, _I, _I, _I, _I, _I, _I, _P], _I),
+    "arc_a8w4_gemm": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P], _I),
+    "arc_a8w4_describe_plan": ([_I, _I, _I, _I, ctypes.POINTER(Plan)], _I),
+    "arc_device_status": ([_I, ctypes.POINTER(ctypes.c_uint32), _I], _I),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded native library (loaded once per process)."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not LIB_PATH.exists():
+                    raise RuntimeError(
+                        f"{LIB_PATH} is not built; the arc GEMMs have no fallback. "
+                        "Build it with `python -m arc.build`.")
+                handle = ctypes.CDLL(str(LIB_PATH))
+                for name, (argtypes, restype) in SIGNATURES.items():
+                    fn = getattr(handle, name)
+                    fn.argtypes = argtypes
+                    fn.restype = restype
+                _lib = handle
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != ARC_OK:
+        L = lib()
+        detail = L.arc_last_error().decode(errors="replace")
+        kind = L.arc_status_string(status).decode(errors="replace")
+        raise ArcError(status, f"{what}: {kind}: {detail}")
+
+
+def describe_plan(M: int, N: int, K: int, num_sms: int = 148) -> dict:
+    """The A8W4 work decomposition for a shape (host-only)."""
+    plan = Plan()
+    check(lib().arc_a8w4_describe_plan(M, N, K, num_sms, ctypes.byref(plan)),
+          "arc_a8w4_describe_plan")
+    return plan.as_dict()
+
+
+def device_status(device: int, clear: bool = True) -> int:
+    """Bit mask of kernel waits that timed out on `device` (synchronises it)."""
+    val = ctypes.c_uint32(0)
+    check(lib().arc_device_status(device, ctypes.byref(val), 1 if clear else 0),
+          "arc_device_status")
+    return int(val.value)
+
+
+def version() -> int:
+    return int(lib().arc_version())

@@ -1,0 +1,100 @@
+"""A8W4 matmul: int8 activations x packed int4 weights with K-group-128 scales.
+
+In the reference this role is played by the third-party call
+`deep_gemm.fp8_fp4_gemm_nt((a, sfa), (b, sfb), out, recipe_a=(1, 128), recipe_b=(1, 32))`
+(tests/a8w4.py:48, :70): operands are (data, scale) pairs, `b` is K-major ("NT") and
+`out` is preallocated by the caller. The same calling shape is kept here for the
+int8 x int4 recipe:
+
+    a = (x,  sa)   x  [M, K]   int8,   sa [M] float32 (one scale per token)
+    b = (wp, sb)   wp [N, K/2] uint8 (two int4 per byte, even k in the low nibble),
+                   sb [N, K/128] bfloat16 (one scale per column and 128-wide K group)
+    out            [M, N] bfloat16
+
+    out[m, n] = bf16( sa[m] * sum_g f32(sb[n, g]) * P[m, n, g] ),
+    P[m, n, g] = sum_{k in group g} x[m, k] * w[n, k]   (int32, exact)
+
+Everything runs in `arc_a8w4_gemm` (include/arc_b200.h) on the caller's stream.
+"""
+from __future__ import annotations
+
+from typing import Sequence
+
+import torch
+
+from ._lib import check, lib
+from .quant import TensorPair
+
+GROUP_K = 128
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _expect(t: torch.Tensor, name: str, dtype: torch.dtype, shape: tuple, device) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor (there is no CPU path), got {t.device}")
+    if device is not None and t.device != device:
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name} must have shape {tuple(shape)}, got {tuple(t.shape)}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def a8w4_matmul(a: TensorPair, b: TensorPair, out: torch.Tensor | None = None, *,
+                group: int = GROUP_K, partials: torch.Tensor | None = None) -> torch.Tensor:
+    """out = A8W4 GEMM of (x, sa) and (wp, sb). See the module docstring.
+
+    `partials`, if given, is an int32 [M, N, K/128] tensor that receives every exact
+    group partial P[m, n, g] (a slow debugging mode).
+    """
+    x, sa = a
+    wp, sb = b
+    m, k = x.shape
+    n, k2 = wp.shape
+    assert k == 2 * k2, f"Inner dimensions must match: {k} vs 2*{k2}"
+    if group != GROUP_K:
+        raise ValueError(f"only group={GROUP_K} is supported, got {group}")
+    assert k % group == 0, f"K ({k}) must be a multiple of {group}"
+    dev = x.device
+    if sa.dim() == 2 and sa.shape[1] == 1:
+        sa = sa.reshape(-1)
+    _expect(x, "a[0]", torch.int8, (m, k), None)
+    _expect(sa, "a[1]", torch.float32, (m,), dev)
+    _expect(wp, "b[0]", torch.uint8, (n, k // 2), dev)
+    _expect(sb, "b[1]", torch.bfloat16, (n, k // group), dev)
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    else:
+        _expect(out, "out", torch.bfloat16, (m, n), dev)
+    pptr = None
+    if partials is not None:
+        _expect(partials, "partials", torch.int32, (m, n, k // group), dev)
+        pptr = partials.data_ptr()
+    with torch.cuda.device(dev):
+        check(lib().arc_a8w4_gemm(x.data_ptr(), sa.data_ptr(), wp.data_ptr(), sb.data_ptr(),
+                                  out.data_ptr(), m, n, k, group, _stream_ptr(dev), pptr),
+              "arc.a8w4_matmul")
+    return out
+
+
+def a8w4_gemm_nt(a: TensorPair, b: TensorPair, out: torch.Tensor,
+                 recipe_a: Sequence[int] | None = None,
+                 recipe_b: Sequence[int] = (1, GROUP_K)) -> torch.Tensor:
+    """deep_gemm-style entry (tests/a8w4.py:48): recipes name the scale granularity.
+
+    recipe_a: None or (1, K) — one activation scale per token.
+    recipe_b: (1, 128)       — one weight scale per column and 128-wide K group.
+    """
+    k = a[0].shape[1]
+    if recipe_a is not None and tuple(recipe_a) != (1, k):
+        raise ValueError(f"recipe_a must be per-token (1, {k}), got {tuple(recipe_a)}")
+    if tuple(recipe_b) != (1, GROUP_K):
+        raise ValueError(f"recipe_b must be (1, {GROUP_K}), got {tuple(recipe_b)}")
+    return a8w4_matmul(a, b, out, group=GROUP_K)

@@ -1,0 +1,115 @@
+/*
+ * arc_b200.h — C ABI of the B200 (sm_100a) GEMM library behind the `arc` Python API.
+ *
+ * The reference binds its GEMM through TVM-FFI: arc/mm.py:30 defines the typed
+ * function `void matmul(TensorView a, TensorView b, TensorView out)` and arc/mm.py:48
+ * exports it (`TVM_FFI_DLL_EXPORT_TYPED_FUNC(matmul, (arc::matmul))`, i.e. the C symbol
+ * `__tvm_ffi_matmul`). Its A8W4 role is the third-party call
+ * `deep_gemm.fp8_fp4_gemm_nt((a, sa), (b, sb), out, recipe_a, recipe_b)` at
+ * tests/a8w4.py:48 and :70. This header replaces both with plain C entry points:
+ * raw device pointers, sizes and a CUDA stream, no framework types.
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are device pointers of the current CUDA device; the caller owns
+ *     every buffer (the reference allocates `out` in Python, arc/mm.py:76-77).
+ *   - Work is enqueued on `stream` and the call returns without synchronising, as the
+ *     reference launches on the caller's stream (arc/mm.py:38,44).
+ *   - The return value is an arc_status_t. Where the reference would exit() the
+ *     process on a CUDA error (arc/include/common.cuh:8-28) or raise an
+ *     AssertionError on a bad shape (arc/mm.py:74-75), these calls return a nonzero
+ *     status instead; arc_last_error() holds a one-line description for the calling
+ *     thread.
+ *   - Kernels never wait without a bound: a pipeline wait that exceeds 2 s records a
+ *     bit in a per-device status word (read with arc_device_status()) and the kernel
+ *     returns.
+ *   - Nothing here allocates device memory.
+ */
+#ifndef ARC_B200_H_
+#define ARC_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *cudaStream_t;
+
+typedef enum arc_status {
+  ARC_OK = 0,
+  ARC_ERR_INVALID_ARGUMENT = 1, /* null pointer, non-positive size, K mismatch */
+  ARC_ERR_UNSUPPORTED = 2,      /* shape/alignment/recipe outside what the kernels cover */
+  ARC_ERR_CUDA = 3,             /* a CUDA runtime or driver call failed */
+  ARC_ERR_NO_DEVICE = 4,        /* no sm_100 device is current */
+  ARC_ERR_DEVICE_TIMEOUT = 5    /* a kernel abandoned a wait (see arc_device_status) */
+} arc_status_t;
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int arc_version(void);
+
+/* Static string for a status code. */
+const char *arc_status_string(int status);
+
+/* Description of the last failure on the calling thread ("" if none). */
+const char *arc_last_error(void);
+
+/*
+ * bf16 GEMM, C[M,N] = A[M,K] . B[N,K]^T with fp32 accumulation and bf16 output.
+ * Replaces: arc/mm.py:30-45 (`arc::matmul` host shim, exported at arc/mm.py:48) and
+ * the kernel arc/include/mm.cuh:31-216.
+ * A, B, C: bf16 (uint16 storage), row-major with leading dimensions lda >= K,
+ * ldb >= K, ldc >= N in elements. Requirements: M, N, K >= 1; base pointers 16-byte
+ * aligned; lda, ldb, ldc multiples of 8. (The reference additionally requires
+ * M % 32 == 0, N % 128 == 0, K % 128 == 0, arc/mm.py:75; those shapes are a subset.)
+ */
+int arc_matmul_bf16(const void *A, const void *B, void *C, int M, int N, int K, int lda,
+                    int ldb, int ldc, cudaStream_t stream);
+
+/*
+ * A8W4 GEMM: int8 activations x packed int4 weights with K-group scales.
+ *   P[m,n,g] = sum_{k in group g} A[m,k] * W[n,k]                  (int32, exact)
+ *   C[m,n]   = bf16( sa[m] * sum_g f32(sb[n,g]) * P[m,n,g] )
+ * Replaces the A8W4 call of the reference, deep_gemm.fp8_fp4_gemm_nt at
+ * tests/a8w4.py:48 / :70 (same NT layout and (data, scale) pairing), with the
+ * int8 x int4 recipe.
+ *   A    [M][K]      int8, contiguous
+ *   sa   [M]         fp32 per-token scale
+ *   Wp   [N][K/2]    uint8; byte j of a row holds w[2j] in bits 3:0 and w[2j+1] in
+ *                    bits 7:4, each a two's-complement int4 (the nibble order of
+ *                    arc/testing/quant.py:82-83)
+ *   sb   [N][K/group] bf16 (uint16 storage)
+ *   C    [M][N]      bf16 (uint16 storage)
+ *   partials_dbg     NULL, or [M][N][K/group] int32 that receives every P[m,n,g]
+ *                    (a slow debugging mode for bit-exact checks)
+ * Requirements: group == 128; K % 128 == 0; M, N >= 1; N % 8 == 0; A, Wp, C 16-byte
+ * aligned.
+ */
+int arc_a8w4_gemm(const int8_t *A, const float *sa, const uint8_t *Wp, const uint16_t *sb,
+                  uint16_t *C, int M, int N, int K, int group, cudaStream_t stream,
+                  int32_t *partials_dbg);
+
+/* The work decomposition arc_a8w4_gemm picks for a shape (host-only, no GPU needed). */
+typedef struct arc_a8w4_plan {
+  int split;        /* 1: K-split clusters with on-chip reduction; 0: persistent tiles */
+  int token_tile;   /* tokens (rows of A) per tile: 16, 32, 64 or 128 */
+  int weight_rows;  /* weight rows (output columns) per tile, <= 128 */
+  int k_split;      /* CTAs per cluster along K (split == 1) */
+  int grid;         /* CTAs launched */
+  int load_stages;  /* depth of the TMA ring */
+} arc_a8w4_plan_t;
+
+int arc_a8w4_describe_plan(int M, int N, int K, int num_sms, arc_a8w4_plan_t *plan);
+
+/*
+ * Device status word of `device`: a bit mask of the pipeline waits that timed out
+ * since it was last cleared (0 = healthy). Synchronises the device. When `clear`
+ * is nonzero the word is reset to 0 after reading.
+ */
+int arc_device_status(int device, uint32_t *status, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ARC_B200_H_ */

@@ -1,0 +1,133 @@
+"""A8W4 parity on the B200: CUDA path through the C ABI vs the CPU oracle.
+
+* int32 group partials: bit-exact against the oracle (tests at sizes it finishes fast);
+* bf16 outputs: within 2 bf16 ulps of the oracle's exact (float64) result;
+* full BASELINE sizes: exact oracle on sampled rows/columns, an fp32 torch reference of
+  the dequantized operands on the GPU for every element, plus size-independent
+  properties (determinism, exact scaling by powers of two in sa).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import arc
+from arc.quant import dequantize_int4
+from arc.testing.data import generate_a8w4
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _bits(sb: torch.Tensor) -> np.ndarray:
+    return sb.view(torch.int16).numpy().view(np.uint16)
+
+
+def _run(dev, m, n, k, seed, with_partials=True):
+    (x, sa), (wp, sb) = generate_a8w4(m, n, k, seed=seed)
+    parts = (torch.full((m, n, k // 128), -12345, dtype=torch.int32, device=dev)
+             if with_partials else None)
+    out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=dev)
+    arc.a8w4_matmul((x.to(dev), sa.to(dev)), (wp.to(dev), sb.to(dev)), out, partials=parts)
+    torch.cuda.synchronize()
+    assert arc.device_status(dev.index or 0) == 0, "kernel reported a wait timeout"
+    return (x, sa, wp, sb), out, parts
+
+
+SHAPES = [
+    (1, 256, 128),      # single token, a single K group
+    (5, 24, 256),       # ragged M, N smaller than one weight tile
+    (16, 4096, 4096),   # the BASELINE decode configuration
+    (16, 1000, 512),    # N not a multiple of the tile height
+    (32, 512, 1024),    # 32-token split-K tile
+    (33, 136, 384),     # first persistent-tile shape (64-token tiles)
+    (64, 264, 640),
+    (100, 264, 256),    # ragged 128-token tiles
+    (256, 1024, 2048),  # several token and weight tiles
+]
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_a8w4_partials_exact_and_outputs(cuda_device, m, n, k):
+    (x, sa, wp, sb), out, parts = _run(cuda_device, m, n, k, seed=m * 7 + n + k)
+    p_ref = oracle.a8w4_partials(x.numpy(), wp.numpy())
+    p_got = parts.cpu().numpy()
+    mism = np.argwhere(p_got != p_ref)
+    assert mism.size == 0, f"{len(mism)} partials differ, first at {tuple(mism[0])}: " \
+                           f"{p_got[tuple(mism[0])]} vs {p_ref[tuple(mism[0])]}"
+    ref = oracle.a8w4_out(x.numpy(), sa.numpy(), wp.numpy(), _bits(sb))
+    ok, msg = oracle.check_bf16_close(out.float().cpu().numpy(), ref, max_ulp=2.0)
+    assert ok, msg
+
+
+@pytest.mark.parametrize("m,n,k", [(16, 4096, 4096), (4096, 14336, 4096)])
+def test_a8w4_baseline_sizes(cuda_device, m, n, k):
+    """Full BASELINE configs: every element vs an fp32 GPU reference, sampled exact oracle."""
+    (x, sa, wp, sb), out, _ = _run(cuda_device, m, n, k, seed=0, with_partials=False)
+    dev = cuda_device
+    # fp32 reference of the dequantized operands (TF32 off: true fp32 products).
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        w_f = dequantize_int4(wp.to(dev), sb.to(dev))
+        a_f = x.to(dev).float() * sa.to(dev).unsqueeze(1)
+        ref32 = (a_f @ w_f.T).double().cpu().numpy()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    ok, msg = oracle.check_bf16_close(out.float().cpu().numpy(), ref32, max_ulp=2.0)
+    assert ok, msg
+    # Exact oracle on a sample of rows and columns.
+    g = np.random.default_rng(1)
+    rows = np.sort(g.choice(m, size=min(m, 48), replace=False))
+    cols = np.sort(g.choice(n, size=min(n, 256), replace=False))
+    ref = oracle.a8w4_out(x.numpy()[rows], sa.numpy()[rows], wp.numpy()[cols],
+                          _bits(sb)[cols])
+    got = out.float().cpu().numpy()[np.ix_(rows, cols)]
+    ok, msg = oracle.check_bf16_close(got, ref, max_ulp=2.0)
+    assert ok, msg
+    # Statistical criterion of the reference's A8W4 check (tests/a8w4.py:53-54).
+    assert oracle.symm_square_rel_L2_error(out.float().cpu().numpy(), ref32) < 1e-4
+
+
+def test_a8w4_deterministic_and_sa_scaling(cuda_device):
+    """Two runs are bit-identical; doubling sa doubles every output exactly."""
+    dev = cuda_device
+    (x, sa), (wp, sb) = generate_a8w4(16, 4096, 4096, seed=5)
+    args = ((x.to(dev), sa.to(dev)), (wp.to(dev), sb.to(dev)))
+    o1 = arc.a8w4_matmul(*args)
+    o2 = arc.a8w4_matmul(*args)
+    o3 = arc.a8w4_matmul((args[0][0], args[0][1] * 2), args[1])
+    torch.cuda.synchronize()
+    assert torch.equal(o1.view(torch.int16), o2.view(torch.int16))
+    assert torch.equal((o1.float() * 2).to(torch.bfloat16).view(torch.int16), o3.view(torch.int16))
+    assert arc.device_status(0) == 0
+
+
+def test_a8w4_extreme_values_exact(cuda_device):
+    """All-extreme operands (int8 -127/127, int4 -8/7): partials at their maximum size."""
+    dev = cuda_device
+    m, n, k = 16, 256, 512
+    x = torch.where(torch.arange(m * k).view(m, k) % 3 == 0, -127, 127).to(torch.int8)
+    w = torch.where(torch.arange(n * k).view(n, k) % 5 == 0, 7, -8).to(torch.int8)
+    wp = arc.quant.pack_int4(w)
+    sa = torch.full((m,), 0.03125)
+    sb = torch.full((n, k // 128), 0.0078125, dtype=torch.bfloat16)
+    parts = torch.empty((m, n, k // 128), dtype=torch.int32, device=dev)
+    out = arc.a8w4_matmul((x.to(dev), sa.to(dev)), (wp.to(dev), sb.to(dev)), partials=parts)
+    torch.cuda.synchronize()
+    assert np.array_equal(parts.cpu().numpy(), oracle.a8w4_partials(x.numpy(), wp.numpy()))
+    ref = oracle.a8w4_out(x.numpy(), sa.numpy(), wp.numpy(), _bits(sb))
+    ok, msg = oracle.check_bf16_close(out.float().cpu().numpy(), ref, max_ulp=2.0)
+    assert ok, msg
+
+
+def test_a8w4_gemm_nt_call_shape(cuda_device):
+    dev = cuda_device
+    (x, sa), (wp, sb) = generate_a8w4(16, 512, 1024, seed=3)
+    out = torch.empty((16, 512), dtype=torch.bfloat16, device=dev)
+    arc.a8w4_gemm_nt((x.to(dev), sa.to(dev)), (wp.to(dev), sb.to(dev)), out,
+                     recipe_a=(1, 1024), recipe_b=(1, 128))
+    ref = arc.a8w4_matmul((x.to(dev), sa.to(dev)), (wp.to(dev), sb.to(dev)))
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))

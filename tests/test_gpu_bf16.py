@@ -1,0 +1,87 @@
+"""bf16 GEMM parity on the B200: CUDA path through the C ABI vs the oracle.
+
+Small and ragged shapes are checked against the CPU oracle (float64 of the bf16
+inputs); the BASELINE sizes against an fp32 GPU reference (TF32 off) of the same
+inputs. The bar is 2 bf16 ulps (rtol ~1e-2).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import arc
+from arc.testing.data import generate_bf16
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    return t.view(torch.int16).numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("m,n,k", [
+    (128, 256, 64),     # exactly one tile, one K block
+    (32, 128, 128),     # the reference's minimum legal shape
+    (1, 8, 8),          # tiny and ragged everywhere
+    (200, 264, 320),    # ragged M, N, K
+    (384, 768, 1000),   # K tail inside a block
+    (1024, 1024, 2048),
+])
+def test_bf16_vs_oracle(cuda_device, m, n, k):
+    a, b = generate_bf16(m, n, k, seed=m + n + k)
+    out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+    arc.matmul(a.to(cuda_device), b.to(cuda_device), out=out)
+    torch.cuda.synchronize()
+    assert arc.device_status(0) == 0
+    ref = oracle.bf16_gemm(_bits(a), _bits(b))
+    ok, msg = oracle.check_bf16_close(out.float().cpu().numpy(), ref,
+                                      atol=oracle.tensor_core_atol(k, ref))
+    assert ok, msg
+
+
+@pytest.mark.parametrize("m,n,k", [(2048, 2048, 2048), (8192, 8192, 8192)])
+def test_bf16_baseline_sizes(cuda_device, m, n, k):
+    dev = cuda_device
+    a, b = generate_bf16(m, n, k, seed=0, device=dev)
+    out = arc.matmul(a, b)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ref = (a.float() @ b.float().T).double().cpu().numpy()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    torch.cuda.synchronize()
+    assert arc.device_status(0) == 0
+    ok, msg = oracle.check_bf16_close(out.float().cpu().numpy(), ref,
+                                      atol=oracle.tensor_core_atol(k, ref))
+    assert ok, msg
+    # Same answer as the vendor GEMM to within the bf16 rounding of each.
+    cub = torch.mm(a, b.T).float().cpu().numpy()
+    assert oracle.symm_square_rel_L2_error(out.float().cpu().numpy(), cub) < 1e-5
+
+
+def test_bf16_strided_operands(cuda_device):
+    """Row pitch larger than K (a column slice of a wider matrix)."""
+    dev = cuda_device
+    a_full, b_full = generate_bf16(256, 384, 512, seed=9, device=dev)
+    a = a_full[:, :448]
+    b = b_full[:, :448]
+    out = arc.matmul(a, b)
+    ref = oracle.bf16_gemm(_bits(a.contiguous().cpu()), _bits(b.contiguous().cpu()))
+    torch.cuda.synchronize()
+    ok, msg = oracle.check_bf16_close(out.float().cpu().numpy(), ref,
+                                      atol=oracle.tensor_core_atol(448, ref))
+    assert ok, msg
+
+
+def test_bf16_out_preallocated_and_deterministic(cuda_device):
+    dev = cuda_device
+    a, b = generate_bf16(512, 512, 512, seed=4, device=dev)
+    o1 = torch.empty((512, 512), dtype=torch.bfloat16, device=dev)
+    r = arc.matmul(a, b, out=o1)
+    o2 = arc.matmul(a, b)
+    torch.cuda.synchronize()
+    assert r.data_ptr() == o1.data_ptr()
+    assert torch.equal(o1.view(torch.int16), o2.view(torch.int16))
