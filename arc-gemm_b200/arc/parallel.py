@@ -48,9 +48,12 @@ def gather_columns(local: torch.Tensor, world: int, group=None) -> torch.Tensor:
     m, nl = local.shape
     if world == 1:
         return local
-    stacked = torch.empty((world, m, nl), dtype=local.dtype, device=local.device)
+    # Rank blocks land one after another along dim 0 ([g*M, N/g], accepted by NCCL
+    # and gloo alike), then are re-laid out so rank r's block becomes columns
+    # [r*N/g, (r+1)*N/g).
+    stacked = torch.empty((world * m, nl), dtype=local.dtype, device=local.device)
     dist.all_gather_into_tensor(stacked, local.contiguous(), group=group)
-    return stacked.permute(1, 0, 2).reshape(m, world * nl)
+    return stacked.view(world, m, nl).permute(1, 0, 2).reshape(m, world * nl)
 
 
 def sharded_gemm(local_gemm: Callable[..., torch.Tensor], a, b_local, *, world: int,

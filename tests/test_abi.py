@@ -1,0 +1,95 @@
+"""CPU: the C-ABI library loads, exports every declared symbol, and validates input.
+
+No compute call reaches a GPU here: every call below is rejected by host-side checks
+that run before any CUDA call, or is a host-only entry point.
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from arc import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "arc_b200.h"
+
+
+def declared_functions() -> set[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return set(re.findall(r"\b(arc_[a-z0-9_]+)\s*\(", text))
+
+
+def test_header_declares_the_bound_symbols():
+    assert declared_functions() == set(_lib.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol(native_lib):
+    for name in declared_functions():
+        assert hasattr(native_lib, name), f"{name} missing from libarcb200.so"
+
+
+def test_version_and_status_strings(native_lib):
+    assert native_lib.arc_version() >= 100
+    assert native_lib.arc_status_string(0) == b"ok"
+    assert b"unsupported" in native_lib.arc_status_string(2)
+    assert native_lib.arc_status_string(99) == b"unknown status"
+
+
+def test_invalid_arguments_are_rejected_before_any_cuda_call(native_lib):
+    L = native_lib
+    nul = None
+    buf = ctypes.create_string_buffer(4096)
+    p = ctypes.cast(buf, ctypes.c_void_p).value
+    # null pointers
+    assert L.arc_matmul_bf16(nul, p, p, 1, 1, 1, 8, 8, 8, nul) == _lib.ARC_ERR_INVALID_ARGUMENT
+    assert b"null" in L.arc_last_error()
+    # non-positive sizes
+    assert L.arc_matmul_bf16(p, p, p, 0, 8, 8, 8, 8, 8, nul) == _lib.ARC_ERR_INVALID_ARGUMENT
+    # leading dimension smaller than K
+    assert L.arc_matmul_bf16(p, p, p, 8, 8, 16, 8, 16, 8, nul) == _lib.ARC_ERR_INVALID_ARGUMENT
+    # leading dimension not a multiple of 8
+    assert L.arc_matmul_bf16(p, p, p, 8, 8, 12, 12, 16, 8, nul) == _lib.ARC_ERR_UNSUPPORTED
+    # A8W4: group other than 128, K not a multiple of 128, N not a multiple of 8
+    assert L.arc_a8w4_gemm(p, p, p, p, p, 16, 64, 256, 64, nul, nul) == _lib.ARC_ERR_UNSUPPORTED
+    assert L.arc_a8w4_gemm(p, p, p, p, p, 16, 64, 200, 128, nul, nul) == _lib.ARC_ERR_UNSUPPORTED
+    assert L.arc_a8w4_gemm(p, p, p, p, p, 16, 60, 256, 128, nul, nul) == _lib.ARC_ERR_UNSUPPORTED
+    assert L.arc_a8w4_gemm(p, nul, p, p, p, 16, 64, 256, 128, nul, nul) == \
+        _lib.ARC_ERR_INVALID_ARGUMENT
+    # misaligned operand
+    assert L.arc_a8w4_gemm(p + 1, p, p, p, p, 16, 64, 256, 128, nul, nul) == _lib.ARC_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("m,n,k,expect", [
+    (16, 4096, 4096, dict(split=1, token_tile=16, weight_rows=112, k_split=4, grid=148)),
+    (1, 28672, 8192, dict(split=1, token_tile=16)),
+    (32, 4096, 4096, dict(split=1, token_tile=32)),
+    (33, 4096, 4096, dict(split=0, token_tile=64)),
+    (4096, 14336, 4096, dict(split=0, token_tile=128, weight_rows=128, grid=148)),
+])
+def test_plans(native_lib, m, n, k, expect):
+    plan = _lib.describe_plan(m, n, k, 148)
+    for key, v in expect.items():
+        assert plan[key] == v, (key, plan)
+    if plan["split"]:
+        assert plan["weight_rows"] % 8 == 0 and plan["weight_rows"] % plan["k_split"] == 0
+        assert plan["k_split"] <= k // 128
+        assert plan["grid"] == -(-n // plan["weight_rows"]) * plan["k_split"]
+
+
+def test_decode_plans_cover_every_row(native_lib):
+    """Every decode plan's tiles cover N, its K split never exceeds the group count."""
+    for n in (8, 24, 256, 1000, 4096, 14336, 28672):
+        for k in (128, 256, 4096, 8192):
+            plan = _lib.describe_plan(16, n, k, 148)
+            assert plan["split"] == 1
+            tiles = plan["grid"] // plan["k_split"]
+            assert tiles * plan["weight_rows"] >= n
+            assert 1 <= plan["k_split"] <= max(1, k // 128)
+
+
+def test_plan_rejects_bad_k(native_lib):
+    with pytest.raises(_lib.ArcError):
+        _lib.describe_plan(16, 64, 200, 148)
