@@ -6,9 +6,10 @@ raises. Building it is `python -m arc.build` (or `__graft_entry__.build()`).
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 
-from .build import LIB_PATH
+from .build import LIB_PATH, PROBE_LIB_PATH
 
 ARC_OK = 0
 ARC_ERR_INVALID_ARGUMENT = 1
@@ -34,6 +35,7 @@ class Plan(ctypes.Structure):
         ("k_split", ctypes.c_int),
         ("grid", ctypes.c_int),
         ("load_stages", ctypes.c_int),
+        ("groups_per_stage", ctypes.c_int),
     ]
 
     def as_dict(self) -> dict:
@@ -51,7 +53,13 @@ SIGNATURES = {
     "arc_a8w4_gemm": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P], _I),
     "arc_a8w4_describe_plan": ([_I, _I, _I, _I, ctypes.POINTER(Plan)], _I),
     "arc_device_status": ([_I, ctypes.POINTER(ctypes.c_uint32), _I], _I),
+    "arc_probe_attach": ([_P, ctypes.c_size_t], _I),
 }
+
+
+def probe_enabled() -> bool:
+    """ARC_PROBE in the environment selects the probe build (as the reference does)."""
+    return "ARC_PROBE" in os.environ
 
 _lib = None
 _lock = threading.Lock()
@@ -63,11 +71,12 @@ def lib() -> ctypes.CDLL:
     if _lib is None:
         with _lock:
             if _lib is None:
-                if not LIB_PATH.exists():
+                path = PROBE_LIB_PATH if probe_enabled() else LIB_PATH
+                if not path.exists():
                     raise RuntimeError(
-                        f"{LIB_PATH} is not built; the arc GEMMs have no fallback. "
-                        "Build it with `python -m arc.build`.")
-                handle = ctypes.CDLL(str(LIB_PATH))
+                        f"{path} is not built; the arc GEMMs have no fallback. "
+                        "Build it with `python -m arc.build` (`--probe` for the probe build).")
+                handle = ctypes.CDLL(str(path))
                 for name, (argtypes, restype) in SIGNATURES.items():
                     fn = getattr(handle, name)
                     fn.argtypes = argtypes
@@ -98,6 +107,15 @@ def device_status(device: int, clear: bool = True) -> int:
     check(lib().arc_device_status(device, ctypes.byref(val), 1 if clear else 0),
           "arc_device_status")
     return int(val.value)
+
+
+def probe_attach(buffer) -> None:
+    """Attach a device buffer (a torch int64 CUDA tensor, or None) for probe stamps."""
+    if buffer is None:
+        check(lib().arc_probe_attach(None, 0), "arc_probe_attach")
+    else:
+        check(lib().arc_probe_attach(buffer.data_ptr(), buffer.numel() * buffer.element_size()),
+              "arc_probe_attach")
 
 
 def version() -> int:

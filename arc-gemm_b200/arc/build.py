@@ -21,10 +21,11 @@ ROOT = PKG_DIR.parent
 CSRC = ROOT / "csrc"
 INCLUDE = ROOT.parent / "include"
 LIB_PATH = PKG_DIR / "libarcb200.so"
+PROBE_LIB_PATH = PKG_DIR / "libarcb200_probe.so"
 STAMP = ROOT / "_build" / "libarcb200.hash"
 
 SOURCES = ["api.cu"]
-HEADERS = ["sm100.cuh", "gemm_bf16.cuh", "gemm_a8w4.cuh"]
+HEADERS = ["sm100.cuh", "gemm_bf16.cuh", "gemm_a8w4.cuh", "gemm_a8w4_decode.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -45,8 +46,8 @@ def find_nvcc() -> str:
     raise RuntimeError("nvcc not found: set NVCC or CUDA_HOME")
 
 
-def source_hash() -> str:
-    h = hashlib.sha256()
+def source_hash(probe: bool = False) -> str:
+    h = hashlib.sha256(b"probe" if probe else b"")
     for name in SOURCES + HEADERS:
         h.update(name.encode())
         h.update((CSRC / name).read_bytes())
@@ -55,29 +56,43 @@ def source_hash() -> str:
     return h.hexdigest()
 
 
-def is_current() -> bool:
-    return LIB_PATH.exists() and STAMP.exists() and STAMP.read_text().strip() == source_hash()
+def _paths(probe: bool):
+    if probe:
+        return PROBE_LIB_PATH, STAMP.with_name("libarcb200_probe.hash")
+    return LIB_PATH, STAMP
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    """Compile libarcb200.so in-tree (next to this file). Returns its path."""
-    if not force and is_current():
-        return LIB_PATH
+def is_current(probe: bool = False) -> bool:
+    lib, stamp = _paths(probe)
+    return lib.exists() and stamp.exists() and stamp.read_text().strip() == source_hash(probe)
+
+
+def build(force: bool = False, verbose: bool = False, probe: bool = False) -> Path:
+    """Compile libarcb200.so in-tree (next to this file). Returns its path.
+
+    probe=True builds libarcb200_probe.so with -DARC_PROBE (pipeline timestamps).
+    """
+    lib, stamp = _paths(probe)
+    if not force and is_current(probe):
+        return lib
     nvcc = find_nvcc()
-    STAMP.parent.mkdir(parents=True, exist_ok=True)
-    tmp = LIB_PATH.with_suffix(".so.tmp")
-    cmd = [nvcc, *NVCC_FLAGS, "-I", str(INCLUDE), "-I", str(CSRC), "-o", str(tmp),
-           *[str(CSRC / s) for s in SOURCES]]
+    stamp.parent.mkdir(parents=True, exist_ok=True)
+    tmp = lib.with_suffix(".so.tmp")
+    cmd = [nvcc, *NVCC_FLAGS, *(["-DARC_PROBE"] if probe else []), "-I", str(INCLUDE),
+           "-I", str(CSRC), "-o", str(tmp), *[str(CSRC / s) for s in SOURCES]]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
     if verbose:
         print(res.stdout + res.stderr)
-    (ROOT / "_build" / "ptxas.log").write_text(res.stdout + res.stderr)
-    tmp.replace(LIB_PATH)
-    STAMP.write_text(source_hash())
-    return LIB_PATH
+    (ROOT / "_build" / ("ptxas_probe.log" if probe else "ptxas.log")).write_text(
+        res.stdout + res.stderr)
+    tmp.replace(lib)
+    stamp.write_text(source_hash(probe))
+    return lib
 
 
 if __name__ == "__main__":
-    print(build(force=True, verbose=True))
+    import sys
+
+    print(build(force=True, verbose=True, probe="--probe" in sys.argv))

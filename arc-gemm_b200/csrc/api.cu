@@ -8,11 +8,13 @@
 // (128,128,128)x3 (arc/mm.py:64).
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
 #include "arc_b200.h"
 #include "gemm_a8w4.cuh"
+#include "gemm_a8w4_decode.cuh"
 #include "gemm_bf16.cuh"
 #include "sm100.cuh"
 
@@ -77,6 +79,27 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t elem_bytes, 
   return ARC_OK;
 }
 
+// A [M][K] byte matrix viewed as [G][M][128]: group g's token tile is the 3-D box
+// {128, rows, groups} at (0, m0, g), landing as consecutive [rows][128] tiles.
+int encode_tokens_3d(CUtensorMap* map, const void* ptr, uint64_t M, uint64_t K, uint32_t box_rows,
+                     uint32_t box_groups) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(ARC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[3] = {128, M, K / 128};
+  const cuuint64_t strides[2] = {K, 128};
+  const cuuint32_t box[3] = {128, box_rows, box_groups};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(ptr), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return fail(ARC_ERR_CUDA, "cuTensorMapEncodeTiled(tokens 3-D) failed with CUresult %d",
+                static_cast<int>(r));
+  }
+  return ARC_OK;
+}
+
 // ---------------------------------------------------------------------------------
 // Per-device facts and one-time kernel attributes.
 // ---------------------------------------------------------------------------------
@@ -86,6 +109,8 @@ struct DeviceState {
   std::once_flag once;
   int status = ARC_OK;
   int sms = 0;
+  int max_clusters2 = 0;  // co-resident 2-CTA clusters of the decode kernel
+  int max_clusters4 = 0;  // co-resident 4-CTA clusters of the decode kernel
 };
 DeviceState g_dev[kMaxDevices];
 
@@ -95,17 +120,20 @@ cudaError_t allow_smem(Kernel k, size_t bytes) {
                               static_cast<int>(bytes));
 }
 
-template <uint32_t BT, uint32_t EWG, uint32_t LS, bool kSplit>
+template <uint32_t BT, uint32_t EWG, uint32_t LS>
 constexpr size_t a8w4_smem_bytes() {
-  return sizeof(arcb::a8w4::Smem<BT, EWG, LS, kSplit>) + 1024;
+  return sizeof(arcb::a8w4::Smem<BT, EWG, LS>) + 1024;
 }
 
-// The kernel instantiations the dispatcher can pick.
+template <uint32_t BT>
+constexpr size_t decode_smem_bytes() {
+  return sizeof(arcb::a8w4dec::Smem<BT>) + 1024;
+}
+
+// The persistent-tile instantiations the dispatcher can pick (M > 32).
 #define ARC_A8W4_VARIANTS(X) \
-  X(16, 1, 8, true)          \
-  X(32, 1, 8, true)          \
-  X(64, 1, 5, false)         \
-  X(128, 2, 4, false)
+  X(64, 1, 5)                \
+  X(128, 2, 4)
 
 int init_device(int dev) {
   DeviceState& st = g_dev[dev];
@@ -123,14 +151,44 @@ int init_device(int dev) {
     }
     st.sms = prop.multiProcessorCount;
     e = allow_smem(arcb::bf16::gemm_bf16_kernel, arcb::bf16::kSmemBytes);
-#define ARC_SET_ATTR(BT, EWG, LS, SPLIT)                                              \
+#define ARC_SET_ATTR(BT, EWG, LS)                                                     \
   if (e == cudaSuccess) {                                                             \
-    e = allow_smem(arcb::a8w4::gemm_a8w4_kernel<BT, EWG, LS, SPLIT>,                  \
-                   a8w4_smem_bytes<BT, EWG, LS, SPLIT>());                            \
+    e = allow_smem(arcb::a8w4::gemm_a8w4_kernel<BT, EWG, LS>,                         \
+                   a8w4_smem_bytes<BT, EWG, LS>());                                   \
   }
     ARC_A8W4_VARIANTS(ARC_SET_ATTR)
 #undef ARC_SET_ATTR
-    if (e != cudaSuccess) st.status = cuda_fail(e, "cudaFuncSetAttribute");
+    if (e == cudaSuccess) {
+      e = allow_smem(arcb::a8w4dec::gemm_a8w4_decode_kernel<16>, decode_smem_bytes<16>());
+    }
+    if (e == cudaSuccess) {
+      e = allow_smem(arcb::a8w4dec::gemm_a8w4_decode_kernel<32>, decode_smem_bytes<32>());
+    }
+    if (e != cudaSuccess) {
+      st.status = cuda_fail(e, "cudaFuncSetAttribute");
+      return;
+    }
+    // How many 2- and 4-CTA clusters of the (larger) decode variant fit at once.
+    for (uint32_t size : {2u, 4u}) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(size * st.sms, 1, 1);
+      cfg.blockDim = dim3(arcb::a8w4dec::kThreads, 1, 1);
+      cfg.dynamicSmemBytes = decode_smem_bytes<32>();
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = size;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, arcb::a8w4dec::gemm_a8w4_decode_kernel<32>, &cfg) !=
+          cudaSuccess) {
+        cudaGetLastError();  // clear; plans then avoid clusters of this size
+        n = 0;
+      }
+      (size == 2 ? st.max_clusters2 : st.max_clusters4) = n;
+    }
   });
   if (st.status != ARC_OK) {
     // Re-state the stored failure for this thread.
@@ -153,34 +211,82 @@ uint32_t ceil_div(uint32_t a, uint32_t b) { return (a + b - 1) / b; }
 // ---------------------------------------------------------------------------------
 // A8W4 work decomposition
 // ---------------------------------------------------------------------------------
-// Decode-sized problems (M <= 32) stream the weights once: the plan chooses a tile
-// height R (multiple of 8, <= 128) and a K-split S so that ceil(N/R)*S CTAs fill the
-// SMs in as few waves as possible, scored by the bytes the busiest SM streams plus a
-// fixed per-wave cost. Larger M uses persistent token x weight tiles.
-int plan_a8w4(int M, int N, int K, int sms, arc_a8w4_plan_t* plan) {
+constexpr uint32_t kDecodeMaxM = 32;
+
+uint32_t decode_stage_bytes(uint32_t bt, uint32_t R, uint32_t gps) {
+  return ceil_div(gps * (bt * arcb::a8w4::kGroupK + R * arcb::a8w4::kPackedRow), 1024) * 1024;
+}
+
+// Groups per ring stage: the largest of 8, 4, 2 for which two stages fit the ring.
+uint32_t decode_gps(uint32_t bt, uint32_t R) {
+  for (uint32_t gps = 8; gps > 2; gps /= 2) {
+    if (arcb::a8w4dec::kRingBytes / decode_stage_bytes(bt, R, gps) >= 2) return gps;
+  }
+  return 2;
+}
+
+uint32_t decode_stages(uint32_t bt, uint32_t R, uint32_t gps) {
+  const uint32_t n = arcb::a8w4dec::kRingBytes / decode_stage_bytes(bt, R, gps);
+  return n < arcb::a8w4dec::kMaxStages ? n : arcb::a8w4dec::kMaxStages;
+}
+
+// Decode-sized problems (M <= 32) stream the weights once. A plan is a tile height R
+// (multiple of 8 in [32, 128]) and a K split S in {1, 2, 4} (S > 1: one wave of
+// S-CTA clusters reducing on chip; S == 1: persistent unsplit tiles). Its estimated
+// time is the largest of
+//   * issuing the CTA's tcgen05.mma instructions (4 per K-group, ~55 cycles each
+//     whatever R is: so tall tiles and K splits pay off),
+//   * streaming the whole weight matrix at HBM speed,
+//   * streaming one CTA's share through one SM,
+// plus a fixed cost for the cluster exchange when S > 1.
+//
+// ARC_DECODE_PLAN="R:S" (tuning and tests only) forces a decode decomposition; it is
+// ignored unless it is valid for the shape and device.
+bool decode_override(uint32_t N, uint32_t G, int sms, int max_c2, int max_c4, uint32_t bt,
+                     arc_a8w4_plan_t* plan);
+
+int plan_a8w4(int M, int N, int K, int sms, int max_c2, int max_c4, arc_a8w4_plan_t* plan) {
   const uint32_t G = static_cast<uint32_t>(K) / arcb::a8w4::kGroupK;
-  if (M <= 32) {
+  if (M <= static_cast<int>(kDecodeMaxM)) {
     const uint32_t bt = M <= 16 ? 16u : 32u;
-    // One "row-group" = 64 bytes of packed weights. ~1400 of them is roughly the
-    // per-SM streaming time of a kernel launch's fixed overhead.
-    constexpr double kWaveCost = 1400.0;
+    if (decode_override(N, G, sms, max_c2, max_c4, bt, plan)) return ARC_OK;
+    constexpr double kGroupIssueNs = 4.0 * 55.0 / 1.9;
+    constexpr double kHbmBytesPerNs = 6500.0;
+    constexpr double kSmBytesPerNs = 120.0;
+    constexpr double kClusterNs = 500.0;
+    const double total_bytes = static_cast<double>(N) * K / 2;
     double best = 1e300;
     arc_a8w4_plan_t bp{};
-    for (uint32_t R = 128; R >= 64; R -= 8) {
-      const uint32_t tiles = ceil_div(static_cast<uint32_t>(N), R);
-      for (uint32_t S = 1; S <= arcb::a8w4::kMaxSplit; S *= 2) {
-        if (S > G || (R % S) != 0) continue;
-        const uint32_t ctas = tiles * S;
-        const uint32_t waves = ceil_div(ctas, static_cast<uint32_t>(sms));
-        const double cost = waves * (static_cast<double>(R) * ceil_div(G, S) + kWaveCost);
-        if (cost < best - 1e-9) {
-          best = cost;
-          bp.split = 1;
+    for (uint32_t S = 1; S <= 4; S *= 2) {
+      if (S > G) continue;
+      const int cap = S == 1 ? 1 << 30 : (S == 2 ? max_c2 : max_c4);
+      for (uint32_t R = 128; R >= 32; R -= 8) {
+        if ((R / S) % 8 || R % S) continue;  // output columns per CTA: 16-byte TMA rows
+        const uint32_t tiles = ceil_div(static_cast<uint32_t>(N), R);
+        uint32_t groups, grid;
+        if (S > 1) {
+          if (tiles > static_cast<uint32_t>(cap)) continue;  // must be one wave
+          groups = ceil_div(G, S);
+          grid = tiles * S;
+        } else {
+          groups = G * ceil_div(tiles, static_cast<uint32_t>(sms));
+          grid = tiles < static_cast<uint32_t>(sms) ? tiles : static_cast<uint32_t>(sms);
+        }
+        const double t_issue = groups * kGroupIssueNs;
+        const double t_sm = static_cast<double>(R) * groups * arcb::a8w4::kPackedRow / kSmBytesPerNs;
+        double t = t_issue > t_sm ? t_issue : t_sm;
+        if (total_bytes / kHbmBytesPerNs > t) t = total_bytes / kHbmBytesPerNs;
+        if (S > 1) t += kClusterNs;
+        if (t < best - 1e-6) {
+          best = t;
+          const uint32_t gps = decode_gps(bt, R);
+          bp.split = S > 1 ? 1 : 0;
           bp.token_tile = static_cast<int>(bt);
           bp.weight_rows = static_cast<int>(R);
           bp.k_split = static_cast<int>(S);
-          bp.grid = static_cast<int>(ctas);
-          bp.load_stages = 8;
+          bp.grid = static_cast<int>(grid);
+          bp.load_stages = static_cast<int>(decode_stages(bt, R, gps));
+          bp.groups_per_stage = static_cast<int>(gps);
         }
       }
     }
@@ -196,28 +302,57 @@ int plan_a8w4(int M, int N, int K, int sms, arc_a8w4_plan_t* plan) {
   plan->k_split = 1;
   plan->grid = static_cast<int>(tiles < static_cast<uint32_t>(sms) ? tiles : sms);
   plan->load_stages = bt == 64 ? 5 : 4;
+  plan->groups_per_stage = 1;
   return ARC_OK;
 }
 
-template <uint32_t BT, uint32_t EWG, uint32_t LS, bool kSplit>
-cudaError_t launch_a8w4(const arcb::a8w4::Params& p, uint32_t grid, uint32_t cluster,
-                        cudaStream_t stream) {
-  using C = arcb::a8w4::Cfg<BT, EWG, LS, kSplit>;
+bool decode_override(uint32_t N, uint32_t G, int sms, int max_c2, int max_c4, uint32_t bt,
+                     arc_a8w4_plan_t* plan) {
+  const char* env = getenv("ARC_DECODE_PLAN");
+  unsigned R = 0, S = 0;
+  if (env == nullptr || sscanf(env, "%u:%u", &R, &S) != 2) return false;
+  if (R < 32 || R > 128 || R % 8 || !(S == 1 || S == 2 || S == 4) || S > G || R % S ||
+      (R / S) % 8) {
+    return false;
+  }
+  const uint32_t tiles = ceil_div(N, R);
+  if (S > 1 && tiles > static_cast<uint32_t>(S == 2 ? max_c2 : max_c4)) return false;
+  const uint32_t gps = decode_gps(bt, R);
+  if (arcb::a8w4dec::kSlotBytes / (R * arcb::a8w4::kGroupK) < gps) return false;
+  plan->split = S > 1 ? 1 : 0;
+  plan->token_tile = static_cast<int>(bt);
+  plan->weight_rows = static_cast<int>(R);
+  plan->k_split = static_cast<int>(S);
+  plan->grid = static_cast<int>(S > 1 ? tiles * S : (tiles < static_cast<uint32_t>(sms) ? tiles : sms));
+  plan->load_stages = static_cast<int>(decode_stages(bt, R, gps));
+  plan->groups_per_stage = static_cast<int>(gps);
+  return true;
+}
+
+// Launch with programmatic stream serialization (PDL) and an optional cluster.
+template <typename Kern, typename P>
+cudaError_t launch_ex(Kern kernel, const P& p, uint32_t grid, uint32_t threads, size_t smem,
+                      uint32_t cluster, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(C::kThreads, 1, 1);
-  cfg.dynamicSmemBytes = a8w4_smem_bytes<BT, EWG, LS, kSplit>();
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  if (kSplit) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = cluster;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+  cudaLaunchAttribute attr[2];
+  uint32_t n = 0;
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+  if (cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
   }
-  return cudaLaunchKernelEx(&cfg, arcb::a8w4::gemm_a8w4_kernel<BT, EWG, LS, kSplit>, p);
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
 }  // namespace
@@ -289,8 +424,8 @@ int arc_matmul_bf16(const void* A, const void* B, void* C, int M, int N, int K, 
   const uint32_t grid = p.num_tiles < static_cast<uint32_t>(g_dev[dev].sms)
                             ? p.num_tiles
                             : static_cast<uint32_t>(g_dev[dev].sms);
-  B16::gemm_bf16_kernel<<<grid, B16::kNumThreads, B16::kSmemBytes, stream>>>(p);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e =
+      launch_ex(B16::gemm_bf16_kernel, p, grid, B16::kNumThreads, B16::kSmemBytes, 1, stream);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_bf16_kernel launch");
   return ARC_OK;
 }
@@ -302,7 +437,8 @@ int arc_a8w4_describe_plan(int M, int N, int K, int num_sms, arc_a8w4_plan_t* pl
   if (K % static_cast<int>(arcb::a8w4::kGroupK) != 0) {
     return fail(ARC_ERR_UNSUPPORTED, "arc_a8w4_describe_plan: K must be a multiple of 128");
   }
-  return plan_a8w4(M, N, K, num_sms, plan);
+  // Without a device: assume clusters of 2 and 4 tile the SMs completely.
+  return plan_a8w4(M, N, K, num_sms, num_sms / 2, num_sms / 4, plan);
 }
 
 int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_t* sb,
@@ -335,9 +471,59 @@ int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uin
   if (int st = current_device(&dev)) return st;
 
   arc_a8w4_plan_t plan;
-  plan_a8w4(M, N, K, g_dev[dev].sms, &plan);
+  plan_a8w4(M, N, K, g_dev[dev].sms, g_dev[dev].max_clusters2, g_dev[dev].max_clusters4, &plan);
   const uint32_t BT = static_cast<uint32_t>(plan.token_tile);
   const uint32_t R = static_cast<uint32_t>(plan.weight_rows);
+  const uint32_t G = static_cast<uint32_t>(K / group);
+  cudaError_t e = cudaErrorInvalidConfiguration;
+  if (M <= static_cast<int>(kDecodeMaxM)) {
+    namespace D = arcb::a8w4dec;
+    D::Params p;
+    const uint32_t gps = static_cast<uint32_t>(plan.groups_per_stage);
+    if (int st = encode_tokens_3d(&p.tm_tok, A, M, K, BT, gps)) return st;
+    // Packed weights as [N][K/8] u32 so one box row spans gps groups (gps*64 bytes).
+    if (int st = encode_2d(&p.tm_wp, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, Wp, K / 8, N, K / 8,
+                           gps * (arcb::a8w4::kPackedRow / 4), R, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           "Wp")) {
+      return st;
+    }
+    const uint32_t S = static_cast<uint32_t>(plan.k_split);
+    if (int st = encode_2d(&p.tm_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, N, M, N, R / S, BT,
+                           CU_TENSOR_MAP_SWIZZLE_NONE, "C")) {
+      return st;
+    }
+    p.sa = sa;
+    p.sb = sb;
+    p.out = C;
+    p.partials = partials_dbg;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.G = G;
+    p.ldsb = G;
+    p.ldc = N;
+    p.R = R;
+    p.S = plan.k_split;
+    p.num_items = ceil_div(N, R);
+    p.gps = gps;
+    p.stage_bytes = decode_stage_bytes(BT, R, gps);
+    p.stages = plan.load_stages;
+    p.tok_bytes = gps * BT * arcb::a8w4::kGroupK;
+    p.slot_stride = R * arcb::a8w4::kGroupK;
+    p.slots = arcb::a8w4dec::kSlotBytes / p.slot_stride;
+    if (p.slots > arcb::a8w4dec::kMaxSlots) p.slots = arcb::a8w4dec::kMaxSlots;
+    if (p.slots < gps) return fail(ARC_ERR_UNSUPPORTED, "decode plan: too few unpack slots");
+    const uint32_t grid = static_cast<uint32_t>(plan.grid);
+    if (BT == 16) {
+      e = launch_ex(D::gemm_a8w4_decode_kernel<16>, p, grid, D::kThreads, decode_smem_bytes<16>(),
+                    p.S, stream);
+    } else {
+      e = launch_ex(D::gemm_a8w4_decode_kernel<32>, p, grid, D::kThreads, decode_smem_bytes<32>(),
+                    p.S, stream);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "gemm_a8w4_decode_kernel launch");
+    return ARC_OK;
+  }
 
   namespace Q = arcb::a8w4;
   Q::Params p;
@@ -349,13 +535,9 @@ int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uin
                          Q::kPackedRow, R, CU_TENSOR_MAP_SWIZZLE_NONE, "Wp")) {
     return st;
   }
-  if (!plan.split) {
-    if (int st = encode_2d(&p.tm_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, N, M, N, Q::kRows,
-                           BT, CU_TENSOR_MAP_SWIZZLE_NONE, "C")) {
-      return st;
-    }
-  } else {
-    memset(&p.tm_out, 0, sizeof(p.tm_out));
+  if (int st = encode_2d(&p.tm_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, N, M, N, Q::kRows, BT,
+                         CU_TENSOR_MAP_SWIZZLE_NONE, "C")) {
+    return st;
   }
   p.sa = sa;
   p.sb = sb;
@@ -364,27 +546,39 @@ int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uin
   p.M = M;
   p.N = N;
   p.K = K;
-  p.G = K / group;
-  p.ldsb = p.G;
+  p.G = G;
+  p.ldsb = G;
   p.ldc = N;
   p.R = R;
-  p.S = plan.k_split;
   p.tiles_m = ceil_div(M, BT);
   p.tiles_n = ceil_div(N, R);
   p.num_tiles = p.tiles_m * p.tiles_n;
-
-  cudaError_t e = cudaErrorInvalidConfiguration;
-  if (plan.split) {
-    const uint32_t grid = p.num_tiles * p.S;
-    if (BT == 16) e = launch_a8w4<16, 1, 8, true>(p, grid, p.S, stream);
-    else e = launch_a8w4<32, 1, 8, true>(p, grid, p.S, stream);
+  const uint32_t grid = static_cast<uint32_t>(plan.grid);
+  if (BT == 64) {
+    e = launch_ex(Q::gemm_a8w4_kernel<64, 1, 5>, p, grid, Q::Cfg<64, 1, 5>::kThreads,
+                  a8w4_smem_bytes<64, 1, 5>(), 1, stream);
   } else {
-    const uint32_t grid = static_cast<uint32_t>(plan.grid);
-    if (BT == 64) e = launch_a8w4<64, 1, 5, false>(p, grid, 1, stream);
-    else e = launch_a8w4<128, 2, 4, false>(p, grid, 1, stream);
+    e = launch_ex(Q::gemm_a8w4_kernel<128, 2, 4>, p, grid, Q::Cfg<128, 2, 4>::kThreads,
+                  a8w4_smem_bytes<128, 2, 4>(), 1, stream);
   }
   if (e != cudaSuccess) return cuda_fail(e, "gemm_a8w4_kernel launch");
   return ARC_OK;
+}
+
+int arc_probe_attach(void* buffer, size_t bytes) {
+#if defined(ARC_PROBE)
+  if (buffer != nullptr && bytes < sizeof(unsigned long long) * arcb::kProbeSlots) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_probe_attach: buffer smaller than one CTA's stamps");
+  }
+  unsigned long long* ptr = static_cast<unsigned long long*>(buffer);
+  const cudaError_t e = cudaMemcpyToSymbol(arcb::g_arc_probe, &ptr, sizeof(ptr));
+  if (e != cudaSuccess) return cuda_fail(e, "arc_probe_attach");
+  return ARC_OK;
+#else
+  (void)buffer;
+  (void)bytes;
+  return fail(ARC_ERR_UNSUPPORTED, "arc_probe_attach: library built without ARC_PROBE");
+#endif
 }
 
 int arc_device_status(int device, uint32_t* status, int clear) {

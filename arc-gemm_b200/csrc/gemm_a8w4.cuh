@@ -35,14 +35,9 @@
 //   warps 4-7     unpack warpgroup: packed smem -> int8 SW128 smem (kUnpackStages ring)
 //   warps 8-...   epilogue warpgroup(s): tcgen05.ld partial, fp32 scale-accumulate
 //
-// Two work decompositions share the kernel body:
-//   kSplit = false  persistent CTAs stride over (token tile, weight tile) pairs; each
-//                   tile covers all K-groups and is stored through TMA.
-//   kSplit = true   decode shapes: a cluster of S CTAs shares one weight tile, each
-//                   CTA takes a contiguous K-group range; the fp32 partial sums are
-//                   reduced across the cluster through distributed shared memory in
-//                   a fixed rank order (deterministic), each CTA finishing a slice
-//                   of the tile's rows.
+// Work decomposition: persistent CTAs stride over (token tile, weight tile) pairs;
+// each tile covers all K-groups and is stored through TMA. Decode-sized M (<= 32)
+// uses the dedicated kernel in gemm_a8w4_decode.cuh instead.
 #pragma once
 
 #include "sm100.cuh"
@@ -55,12 +50,11 @@ constexpr uint32_t kGroupK = 128;      // K elements per scale group = one 128-b
 constexpr uint32_t kPackedRow = 64;    // bytes of packed int4 per row per group
 constexpr uint32_t kUmmaK = 32;        // K per kind::i8 UMMA (32 bytes)
 constexpr uint32_t kUnpackStages = 3;
-constexpr uint32_t kMaxSplit = 8;
 
 struct Params {
   CUtensorMap tm_tok;  // A  [M][K] u8 view of int8, box {128, BT}, SW128
   CUtensorMap tm_wp;   // Wp [N][K/2] u8, box {64, R}, no swizzle
-  CUtensorMap tm_out;  // out [M][N] bf16, box {128, BT}, no swizzle (kSplit == false)
+  CUtensorMap tm_out;  // out [M][N] bf16, box {128, BT}, no swizzle
   const float* sa;
   const uint16_t* sb;
   uint16_t* out;
@@ -69,11 +63,10 @@ struct Params {
   uint32_t ldsb;       // elements between sb rows
   uint32_t ldc;        // elements between out rows
   uint32_t R;          // valid weight rows per tile (multiple of 8, <= 128)
-  uint32_t S;          // CTAs per cluster along K (kSplit == true)
   uint32_t tiles_m, tiles_n, num_tiles;
 };
 
-template <uint32_t BT, uint32_t EWG, uint32_t LS, bool kSplit>
+template <uint32_t BT, uint32_t EWG, uint32_t LS>
 struct Cfg {
   static_assert(BT == 16 || BT == 32 || BT == 64 || BT == 128, "token tile");
   static_assert(EWG == 1 || EWG == 2, "epilogue warpgroups");
@@ -85,17 +78,15 @@ struct Cfg {
   static constexpr uint32_t kTokBytes = BT * kGroupK;
   static constexpr uint32_t kWpBytes = kRows * kPackedRow;
   static constexpr uint32_t kWBytes = kRows * kGroupK;
-  static constexpr uint32_t kPartStride = BT + 4;           // floats per partial row (padded)
 };
 
-template <uint32_t BT, uint32_t EWG, uint32_t LS, bool kSplit>
+template <uint32_t BT, uint32_t EWG, uint32_t LS>
 struct alignas(1024) Smem {
-  using C = Cfg<BT, EWG, LS, kSplit>;
+  using C = Cfg<BT, EWG, LS>;
   uint8_t w[kUnpackStages][C::kWBytes];         // unpacked int8, SW128 (UMMA A)
   uint8_t tok[LS][C::kTokBytes];                // tokens, SW128 (UMMA B)
   uint8_t wp[LS][C::kWpBytes];                  // packed int4 straight from TMA
-  // Output staging [BT][128] bf16 (non-split) or fp32 partials [128][BT+4] (split).
-  uint8_t out[kSplit ? kRows * C::kPartStride * 4 : BT * kRows * 2];
+  uint8_t out[BT * kRows * 2];                  // output staging [BT][128] bf16
   float sa[BT];
   uint64_t load_full[LS];
   uint64_t load_empty[LS];
@@ -129,31 +120,18 @@ __device__ __forceinline__ void tile_of(const Params& p, uint32_t t, uint32_t& m
   nt = rem / m_cnt;
 }
 
-template <uint32_t BT, bool kSplit>
+template <uint32_t BT>
 __device__ __forceinline__ bool next_work(const Params& p, uint32_t& cursor, Work& w) {
-  if constexpr (kSplit) {
-    if (cursor != 0) return false;
-    cursor = 1;
-    const uint32_t rank = blockIdx.x % p.S;
-    const uint32_t t = blockIdx.x / p.S;
-    const uint32_t mt = t / p.tiles_n, nt = t % p.tiles_n;
-    w.m0 = mt * BT;
-    w.n0 = nt * p.R;
-    w.g_begin = rank * p.G / p.S;
-    w.g_end = (rank + 1) * p.G / p.S;
-    return true;
-  } else {
-    const uint32_t t = blockIdx.x + cursor * gridDim.x;
-    if (t >= p.num_tiles) return false;
-    ++cursor;
-    uint32_t mt, nt;
-    tile_of(p, t, mt, nt);
-    w.m0 = mt * BT;
-    w.n0 = nt * p.R;
-    w.g_begin = 0;
-    w.g_end = p.G;
-    return true;
-  }
+  const uint32_t t = blockIdx.x + cursor * gridDim.x;
+  if (t >= p.num_tiles) return false;
+  ++cursor;
+  uint32_t mt, nt;
+  tile_of(p, t, mt, nt);
+  w.m0 = mt * BT;
+  w.n0 = nt * p.R;
+  w.g_begin = 0;
+  w.g_end = p.G;
+  return true;
 }
 
 // int4 pair-packed bytes -> int8 with each code in the high nibble (value 16*w).
@@ -165,44 +143,24 @@ __device__ __forceinline__ uint2 expand_int4x8(uint32_t x) {
 }
 
 // ---------------------------------------------------------------------------------
-// Cluster helpers (kSplit)
-// ---------------------------------------------------------------------------------
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                   : "memory");
-}
-
-__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
-  uint32_t out;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
-  return out;
-}
-
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
-}
-
-// ---------------------------------------------------------------------------------
 // Kernel
 // ---------------------------------------------------------------------------------
-template <uint32_t BT, uint32_t EWG, uint32_t LS, bool kSplit>
-__global__ void __launch_bounds__(Cfg<BT, EWG, LS, kSplit>::kThreads, 1)
+template <uint32_t BT, uint32_t EWG, uint32_t LS>
+__global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
     gemm_a8w4_kernel(const __grid_constant__ Params p) {
-  using C = Cfg<BT, EWG, LS, kSplit>;
-  using S_t = Smem<BT, EWG, LS, kSplit>;
-  extern __shared__ uint8_t smem_raw[];
-  S_t& s = *reinterpret_cast<S_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                   ~static_cast<uintptr_t>(1023));
+  using C = Cfg<BT, EWG, LS>;
+  using S_t = Smem<BT, EWG, LS>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  S_t& s = *reinterpret_cast<S_t*>(smem_raw + smem_align_pad(smem_raw));
   const uint32_t warp = warp_idx_sync();
   const uint32_t lane = threadIdx.x & 31u;
   volatile uint32_t* abort = &s.abort;
 
+  pdl_launch_dependents();
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&p.tm_tok);
     tma_prefetch_desc(&p.tm_wp);
-    if (!kSplit) tma_prefetch_desc(&p.tm_out);
+    tma_prefetch_desc(&p.tm_out);
     for (uint32_t i = 0; i < LS; ++i) {
       mbar_init(&s.load_full[i], 1);
       mbar_init(&s.load_empty[i], 2);  // MMA commit (tokens) + unpack warpgroup (packed W)
@@ -226,6 +184,9 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS, kSplit>::kThreads, 1)
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
+  // The prologue above may overlap the previous grid in the stream (programmatic
+  // dependent launch); global memory is only touched after it has completed.
+  pdl_wait();
   const uint32_t tmem_base = s.tmem_base;
 
   if (warp == 0) {
@@ -235,7 +196,7 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS, kSplit>::kThreads, 1)
       const uint32_t tx = C::kTokBytes + p.R * kPackedRow;
       Work w;
       bool ok = true;
-      while (ok && next_work<BT, kSplit>(p, cursor, w)) {
+      while (ok && next_work<BT>(p, cursor, w)) {
         for (uint32_t g = w.g_begin; g < w.g_end; ++g) {
           if (!mbar_wait(&s.load_empty[stage], phase ^ 1u, abort, kStatusTimeoutProducer)) {
             ok = false;
@@ -265,7 +226,7 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS, kSplit>::kThreads, 1)
       uint32_t stage = 0, phase = 0, ustage = 0, uphase = 0, gi = 0, cursor = 0;
       Work w;
       bool ok = true;
-      while (ok && next_work<BT, kSplit>(p, cursor, w)) {
+      while (ok && next_work<BT>(p, cursor, w)) {
         for (uint32_t g = w.g_begin; g < w.g_end; ++g, ++gi) {
           const uint32_t acc = gi & 1u;
           const uint32_t acc_phase = (gi >> 1) & 1u;
@@ -306,7 +267,7 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS, kSplit>::kThreads, 1)
     uint32_t stage = 0, phase = 0, ustage = 0, uphase = 0, cursor = 0;
     Work w;
     bool ok = true;
-    while (ok && next_work<BT, kSplit>(p, cursor, w)) {
+    while (ok && next_work<BT>(p, cursor, w)) {
       for (uint32_t g = w.g_begin; g < w.g_end; ++g) {
         if (ut == 0) {
           s.unpack_ok = (mbar_wait(&s.load_full[stage], phase, abort, kStatusTimeoutUnpack) &&
@@ -363,7 +324,7 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS, kSplit>::kThreads, 1)
     uint32_t gi = 0, cursor = 0;
     Work w;
     bool ok = true;
-    while (ok && next_work<BT, kSplit>(p, cursor, w)) {
+    while (ok && next_work<BT>(p, cursor, w)) {
       const uint32_t n = w.n0 + nl;
       const bool n_valid = (nl < p.R) && (n < p.N);
       float acc[C::kCols];
@@ -425,7 +386,7 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS, kSplit>::kThreads, 1)
       }
       if (!ok) break;
 
-      if constexpr (!kSplit) {
+      {
         // ---- scale by sa, stage [BT][128] bf16, one TMA store per tile.
         if (et < BT) s.sa[et] = (w.m0 + et < p.M) ? __ldg(p.sa + w.m0 + et) : 0.f;
         if (et == 0) tma_store_wait_read<0>();  // previous tile's store has read s.out
@@ -442,56 +403,9 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS, kSplit>::kThreads, 1)
           tma_store_2d(&p.tm_out, s.out, int32_t(w.n0), int32_t(w.m0));
           tma_store_commit();
         }
-      } else {
-        // ---- split-K: publish this CTA's fp32 partial [R][BT] for the cluster.
-        float* part = reinterpret_cast<float*>(s.out);
-#pragma unroll
-        for (uint32_t j = 0; j < C::kCols; j += 4) {
-          *reinterpret_cast<float4*>(part + nl * C::kPartStride + col0 + j) =
-              make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-        }
-        if (et < BT) s.sa[et] = (w.m0 + et < p.M) ? __ldg(p.sa + w.m0 + et) : 0.f;
       }
     }
-    if (!kSplit && et == 0) tma_store_wait_all<0>();
-  }
-
-  if constexpr (kSplit) {
-    // Every thread of every CTA in the cluster passes both cluster barriers exactly
-    // once (all earlier waits are bounded), so no CTA leaves while a peer may still
-    // read its partials.
-    __syncwarp();
-    cluster_sync_all();
-    if (warp >= 8 && *abort == 0u) {
-      const uint32_t et = threadIdx.x - 256;
-      const uint32_t rank = blockIdx.x % p.S;
-      const uint32_t rows = p.R / p.S;   // host guarantees R % S == 0
-      const uint32_t r0 = rank * rows;
-      const uint32_t t = blockIdx.x / p.S;
-      const uint32_t m0 = (t / p.tiles_n) * BT, n0 = (t % p.tiles_n) * p.R;
-      const float* part = reinterpret_cast<const float*>(s.out);
-      uint32_t peer_base[kMaxSplit];
-#pragma unroll
-      for (uint32_t q = 0; q < kMaxSplit; ++q) {
-        peer_base[q] = q < p.S ? map_to_rank(part, q) : 0u;
-      }
-      for (uint32_t e = et; e < rows * BT; e += 128 * EWG) {
-        const uint32_t i = e % rows, j = e / rows;
-        const uint32_t nl = r0 + i;
-        const uint32_t off = (nl * Cfg<BT, EWG, LS, kSplit>::kPartStride + j) * 4u;
-        // Fixed rank order 0..S-1: the result does not depend on arrival timing.
-        float sum = 0.f;
-#pragma unroll
-        for (uint32_t q = 0; q < kMaxSplit; ++q) {
-          if (q < p.S) sum += ld_dsmem_f32(peer_base[q] + off);
-        }
-        const uint32_t m = m0 + j, n = n0 + nl;
-        if (m < p.M && n < p.N) {
-          p.out[size_t(m) * p.ldc + n] = __bfloat16_as_ushort(__float2bfloat16_rn(sum * s.sa[j]));
-        }
-      }
-    }
-    cluster_sync_all();
+    if (et == 0) tma_store_wait_all<0>();
   }
 
   tc_fence_before_sync();

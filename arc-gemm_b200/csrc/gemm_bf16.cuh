@@ -67,13 +67,13 @@ __device__ __forceinline__ void tile_coords(const Params& p, uint32_t t, uint32_
 
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                     ~static_cast<uintptr_t>(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>(smem_raw + smem_align_pad(smem_raw));
   const uint32_t warp = warp_idx_sync();
   const uint32_t lane = threadIdx.x & 31u;
   volatile uint32_t* abort = &s.abort;
 
+  pdl_launch_dependents();
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&p.tm_a);
     tma_prefetch_desc(&p.tm_b);
@@ -97,6 +97,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
+  // The prologue above may overlap the previous grid in the stream (programmatic
+  // dependent launch); global memory is only touched after it has completed.
+  pdl_wait();
   const uint32_t tmem_base = s.tmem_base;
 
   if (warp == 0) {

@@ -44,8 +44,43 @@ __device__ uint32_t g_arc_status;
 // milliseconds), far below anything that would look like a hung GPU.
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
 
+// ---------------------------------------------------------------------------------
+// Probe build (-DARC_PROBE): per-CTA %clock64 stamps (SM cycles; compare only
+// within one CTA) at pipeline milestones,
+// written to a device buffer attached with arc_probe_attach(). The reference's
+// equivalent prints %clock64 stamps from the kernel (arc/include/common.cuh:30-39,
+// arc/include/mm.cuh:201-211, selected by the ARC_PROBE environment variable).
+// ---------------------------------------------------------------------------------
+constexpr uint32_t kProbeSlots = 64;  // stamps per CTA
+__device__ unsigned long long* g_arc_probe;
+
+// The buffer pointer is read once per thread (the first stamp); later stamps are a
+// clock read and a store, so they barely perturb the pipeline they measure.
+__device__ __forceinline__ void probe_mark(uint32_t slot) {
+#if defined(ARC_PROBE)
+  __shared__ unsigned long long* cached;  // one copy per CTA, set by the first stamp
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(t));
+  unsigned long long* buf = *reinterpret_cast<unsigned long long* volatile*>(&cached);
+  if (buf == nullptr) {
+    buf = g_arc_probe;
+    cached = buf;
+  }
+  if (buf != nullptr && slot < kProbeSlots) buf[blockIdx.x * kProbeSlots + slot] = t;
+#else
+  (void)slot;
+#endif
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Bytes to skip from the dynamic shared-memory base to the next 1024-byte boundary
+// (the 128-byte swizzle atoms need it). Used as `smem_raw + pad` so the compiler
+// still sees a shared-memory pointer and emits shared (not generic) loads/stores.
+__device__ __forceinline__ uint32_t smem_align_pad(const void* base) {
+  return (1024u - (smem_u32(base) & 1023u)) & 1023u;
 }
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
@@ -102,6 +137,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Same test, but the thread may sleep up to `hint_ns` waiting for the phase (it is
+// woken when the phase completes), so waiting warps leave the issue slots to the
+// warps doing work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase with parity `parity` to complete.
 // Returns false when the wait was abandoned: either this thread timed out (it then
 // raises *abort and ORs `err_bit` into the device status word) or another role of
@@ -113,7 +164,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   const uint64_t start = globaltimer_ns();
 #pragma unroll 1
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(addr, parity)) return true;
+    if (mbar_try_wait_sleep(addr, parity, 20000u)) return true;
     if ((it & 15u) == 0u) {
       if (*abort) return false;
       if (globaltimer_ns() - start > kWaitTimeoutNs) {
@@ -173,6 +224,17 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::"
       "cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y),
+      "l"(cache_hint)
+      : "memory");
+}
+
+// 3-D tiled load (coordinates innermost first), same completion mechanism.
+__device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* dst,
+                                            int32_t x, int32_t y, int32_t z, uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::"
+      "cache_hint [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z),
       "l"(cache_hint)
       : "memory");
 }
@@ -343,6 +405,49 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t m, uint32_t n) {
 __host__ __device__ constexpr uint32_t idesc_s8_s32(uint32_t m, uint32_t n) {
   return make_idesc(2, 1, 1, m, n);
 }
+
+// ---------------------------------------------------------------------------------
+// Thread-block clusters
+// ---------------------------------------------------------------------------------
+// All threads of all CTAs of the cluster; release/acquire orders shared-memory
+// writes before the barrier with distributed-shared-memory reads after it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+// Address of the same shared-memory object in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// Bulk copy of `bytes` (a multiple of 16) from this CTA's shared memory into the
+// shared memory of a CTA of the cluster. `dst` and `remote_bar` are shared::cluster
+// addresses (map_to_rank); the bytes complete as transaction count on remote_bar.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, const void* src, uint32_t bytes,
+                                                  uint32_t remote_bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+      "[%3];" ::"r"(dst),
+      "r"(smem_u32(src)), "r"(bytes), "r"(remote_bar)
+      : "memory");
+}
+
+// Programmatic dependent launch: let the next grid in the stream start its
+// prologue, and wait for the previous grid's completion (and memory) before
+// touching global memory.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------------
 // Numeric helpers

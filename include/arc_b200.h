@@ -97,9 +97,21 @@ typedef struct arc_a8w4_plan {
   int k_split;      /* CTAs per cluster along K (split == 1) */
   int grid;         /* CTAs launched */
   int load_stages;  /* depth of the TMA ring */
+  int groups_per_stage; /* K-groups fetched per ring stage */
 } arc_a8w4_plan_t;
 
 int arc_a8w4_describe_plan(int M, int N, int K, int num_sms, arc_a8w4_plan_t *plan);
+
+/*
+ * Probe builds only (libarcb200_probe.so, compiled with -DARC_PROBE and loaded by the
+ * Python package when the ARC_PROBE environment variable is set). Attaches a device
+ * buffer of at least 64 uint64 per CTA; every kernel launched afterwards on the
+ * current device writes %clock64 stamps (SM cycles, comparable within one CTA) of
+ * its pipeline milestones into buffer[blockIdx.x * 64 + slot]. NULL detaches. Replaces the reference's probe mode
+ * (arc/mm.py:60-65, arc/include/common.cuh:30-39, stamps printed at
+ * arc/include/mm.cuh:201-211). Returns ARC_ERR_UNSUPPORTED in regular builds.
+ */
+int arc_probe_attach(void *buffer, size_t bytes);
 
 /*
  * Device status word of `device`: a bit mask of the pipeline waits that timed out

@@ -63,8 +63,10 @@ def test_invalid_arguments_are_rejected_before_any_cuda_call(native_lib):
 
 
 @pytest.mark.parametrize("m,n,k,expect", [
-    (16, 4096, 4096, dict(split=1, token_tile=16, weight_rows=112, k_split=4, grid=148)),
-    (1, 28672, 8192, dict(split=1, token_tile=16)),
+    # decode: 32 full-height tiles, K split four ways in 4-CTA clusters (one wave)
+    (16, 4096, 4096, dict(split=1, token_tile=16, weight_rows=128, k_split=4, grid=128)),
+    # large N: persistent unsplit 128-row tiles
+    (1, 28672, 8192, dict(split=0, token_tile=16, weight_rows=128, grid=148)),
     (32, 4096, 4096, dict(split=1, token_tile=32)),
     (33, 4096, 4096, dict(split=0, token_tile=64)),
     (4096, 14336, 4096, dict(split=0, token_tile=128, weight_rows=128, grid=148)),
@@ -73,19 +75,30 @@ def test_plans(native_lib, m, n, k, expect):
     plan = _lib.describe_plan(m, n, k, 148)
     for key, v in expect.items():
         assert plan[key] == v, (key, plan)
-    if plan["split"]:
-        assert plan["weight_rows"] % 8 == 0 and plan["weight_rows"] % plan["k_split"] == 0
-        assert plan["k_split"] <= k // 128
-        assert plan["grid"] == -(-n // plan["weight_rows"]) * plan["k_split"]
+    if m <= 32:
+        assert plan["weight_rows"] % 8 == 0 and (plan["weight_rows"] // plan["k_split"]) % 8 == 0
+        assert plan["k_split"] in (1, 2, 4) and plan["k_split"] <= k // 128
+        tiles = -(-n // plan["weight_rows"])
+        if plan["split"]:
+            assert plan["grid"] == tiles * plan["k_split"] <= 148
+        else:
+            assert plan["grid"] == min(tiles, 148)
+        # a ring stage is gps token tiles plus gps*64 bytes of each packed row, 1 KB
+        # aligned; gps is the largest of 8, 4, 2 for which two stages fit the 88 KB ring
+        def stage(gps):
+            raw = gps * (plan["token_tile"] * 128 + plan["weight_rows"] * 64)
+            return -(-raw // 1024) * 1024
+        gps = next((g for g in (8, 4) if 88 * 1024 // stage(g) >= 2), 2)
+        assert plan["groups_per_stage"] == gps
+        assert plan["load_stages"] == min(8, 88 * 1024 // stage(gps)) >= 2
 
 
 def test_decode_plans_cover_every_row(native_lib):
-    """Every decode plan's tiles cover N, its K split never exceeds the group count."""
+    """Every decode plan's tiles cover N and its K split never exceeds the group count."""
     for n in (8, 24, 256, 1000, 4096, 14336, 28672):
         for k in (128, 256, 4096, 8192):
             plan = _lib.describe_plan(16, n, k, 148)
-            assert plan["split"] == 1
-            tiles = plan["grid"] // plan["k_split"]
+            tiles = plan["grid"] // plan["k_split"] if plan["split"] else -(-n // plan["weight_rows"])
             assert tiles * plan["weight_rows"] >= n
             assert 1 <= plan["k_split"] <= max(1, k // 128)
 

@@ -131,3 +131,54 @@ def test_a8w4_gemm_nt_call_shape(cuda_device):
     ref = arc.a8w4_matmul((x.to(dev), sa.to(dev)), (wp.to(dev), sb.to(dev)))
     torch.cuda.synchronize()
     assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+
+
+def _check_on_device(out: torch.Tensor, ref: torch.Tensor, max_ulp: float = 2.0):
+    """check_bf16_close evaluated on the GPU (for outputs too large to copy out)."""
+    ref = ref.double()
+    got = out.double()
+    ulp = torch.exp2(torch.floor(torch.log2(ref.abs().clamp_min(2.0 ** -126))) - 7)
+    atol = float(ref.pow(2).mean().sqrt()) * 2.0 ** -12
+    err = (got - ref).abs()
+    bad = err > max_ulp * ulp + atol
+    n_bad = int(bad.sum())
+    assert n_bad == 0, f"{n_bad} of {ref.numel()} elements beyond {max_ulp} ulp + {atol:.3g}"
+
+
+@pytest.mark.parametrize("m", [1, 16, 128, 1024])
+def test_a8w4_large_weight_sweep(cuda_device, m):
+    """N=28672, K=8192 at the sweep's token counts."""
+    n, k = 28672, 8192
+    dev = cuda_device
+    (x, sa), (wp, sb) = generate_a8w4(m, n, k, seed=m)
+    xd, sad, wpd, sbd = x.to(dev), sa.to(dev), wp.to(dev), sb.to(dev)
+    out = arc.a8w4_matmul((xd, sad), (wpd, sbd))
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ref32 = (xd.float() * sad.unsqueeze(1)) @ dequantize_int4(wpd, sbd).T
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    torch.cuda.synchronize()
+    assert arc.device_status(0) == 0
+    _check_on_device(out, ref32)
+    g = np.random.default_rng(2)
+    rows = np.sort(g.choice(m, size=min(m, 8), replace=False))
+    cols = np.sort(g.choice(n, size=128, replace=False))
+    ref = oracle.a8w4_out(x.numpy()[rows], sa.numpy()[rows], wp.numpy()[cols], _bits(sb)[cols])
+    got = out.float().cpu().numpy()[np.ix_(rows, cols)]
+    ok, msg = oracle.check_bf16_close(got, ref, max_ulp=2.0)
+    assert ok, msg
+
+
+@pytest.mark.parametrize("plan", ["128:4", "128:2", "64:2", "96:4", "64:1", "32:1", "104:1", "48:2"])
+def test_a8w4_decode_decompositions(cuda_device, monkeypatch, plan):
+    """Every decode decomposition (tile height R, K split S) is exact; forced per test."""
+    monkeypatch.setenv("ARC_DECODE_PLAN", plan)
+    R, S = (int(v) for v in plan.split(":"))
+    for m, n, k in ((16, 1000, 1024), (3, 512, 2048), (32, 256, 512)):
+        (x, sa, wp, sb), out, parts = _run(cuda_device, m, n, k, seed=R + S + m)
+        assert np.array_equal(parts.cpu().numpy(), oracle.a8w4_partials(x.numpy(), wp.numpy()))
+        ref = oracle.a8w4_out(x.numpy(), sa.numpy(), wp.numpy(), _bits(sb))
+        ok, msg = oracle.check_bf16_close(out.float().cpu().numpy(), ref, max_ulp=2.0)
+        assert ok, f"plan {plan} {m}x{n}x{k}: {msg}"
