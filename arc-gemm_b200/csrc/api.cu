@@ -240,8 +240,9 @@ uint32_t decode_stages(uint32_t bt, uint32_t R, uint32_t gps) {
 //   * streaming one CTA's share through one SM,
 // plus a fixed cost for the cluster exchange when S > 1.
 //
-// ARC_DECODE_PLAN="R:S" (tuning and tests only) forces a decode decomposition; it is
-// ignored unless it is valid for the shape and device.
+// ARC_DECODE_PLAN="R:S[:GPS]" (tuning and tests only) forces a decode decomposition
+// (and optionally the K-groups per ring stage); it is ignored unless it is valid for
+// the shape and device.
 bool decode_override(uint32_t N, uint32_t G, int sms, int max_c2, int max_c4, uint32_t bt,
                      arc_a8w4_plan_t* plan);
 
@@ -309,15 +310,19 @@ int plan_a8w4(int M, int N, int K, int sms, int max_c2, int max_c4, arc_a8w4_pla
 bool decode_override(uint32_t N, uint32_t G, int sms, int max_c2, int max_c4, uint32_t bt,
                      arc_a8w4_plan_t* plan) {
   const char* env = getenv("ARC_DECODE_PLAN");
-  unsigned R = 0, S = 0;
-  if (env == nullptr || sscanf(env, "%u:%u", &R, &S) != 2) return false;
+  unsigned R = 0, S = 0, gps_req = 0;
+  if (env == nullptr || sscanf(env, "%u:%u:%u", &R, &S, &gps_req) < 2) return false;
   if (R < 32 || R > 128 || R % 8 || !(S == 1 || S == 2 || S == 4) || S > G || R % S ||
       (R / S) % 8) {
     return false;
   }
   const uint32_t tiles = ceil_div(N, R);
   if (S > 1 && tiles > static_cast<uint32_t>(S == 2 ? max_c2 : max_c4)) return false;
-  const uint32_t gps = decode_gps(bt, R);
+  uint32_t gps = decode_gps(bt, R);
+  if (gps_req == 2 || gps_req == 4 || gps_req == 8) {
+    if (arcb::a8w4dec::kRingBytes / decode_stage_bytes(bt, R, gps_req) < 2) return false;
+    gps = gps_req;
+  }
   if (arcb::a8w4dec::kSlotBytes / (R * arcb::a8w4::kGroupK) < gps) return false;
   plan->split = S > 1 ? 1 : 0;
   plan->token_tile = static_cast<int>(bt);
