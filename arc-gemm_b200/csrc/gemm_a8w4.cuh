@@ -27,13 +27,15 @@
 //
 // Roles (256 + 128*EWG threads):
 //   warp 0        TMA producer: token tile [BT x 128 B] (SW128) + packed weight tile
-//                 [R x 64 B] per K-group into a kLoadStages ring
+//                 [R x 64 B] per K-group into stage s of an LS-stage ring
 //   warp 1        UMMA issuer: 4 x tcgen05.mma kind::i8 M=128 N=BT K=32 per group into
-//                 one of two TMEM accumulators (a fresh int32 partial per group)
+//                 one of two TMEM accumulators (a fresh int32 partial per group, on
+//                 top of the bias described at kBiasBits); two commits per group
 //   warp 2        TMEM allocator
 //   warp 3        idle
-//   warps 4-7     unpack warpgroup: packed smem -> int8 SW128 smem (kUnpackStages ring)
-//   warps 8-...   epilogue warpgroup(s): tcgen05.ld partial, fp32 scale-accumulate
+//   warps 4-7     unpack warpgroup: packed smem -> int8 SW128 smem in the same stage
+//   warps 8-...   epilogue warpgroup(s): tcgen05.ld partial, re-arm the bias, fp32
+//                 scale-accumulate on packed f32x2 pairs
 //
 // Work decomposition: persistent CTAs stride over (token tile, weight tile) pairs;
 // each tile covers all K-groups and is stored through TMA. Decode-sized M (<= 32)
@@ -49,7 +51,19 @@ constexpr uint32_t kRows = 128;        // UMMA M: weight rows per tile (TMEM lan
 constexpr uint32_t kGroupK = 128;      // K elements per scale group = one 128-byte row
 constexpr uint32_t kPackedRow = 64;    // bytes of packed int4 per row per group
 constexpr uint32_t kUmmaK = 32;        // K per kind::i8 UMMA (32 bytes)
-constexpr uint32_t kUnpackStages = 3;
+// Accumulator bias. Between uses every int32 accumulator column in TMEM holds
+// kBiasBits, the bit pattern of kBiasF = 1.5 * 2^23, and the UMMAs of a K-group
+// accumulate onto it. Since |16 P| < 2^22, the int32 sum kBiasBits + 16P is exactly
+// the bit pattern of the float kBiasF + 16P, so a partial is read back as a float with
+// no int->float conversion instruction (those issue on a quarter-rate pipe and would
+// cap the kernel far below the tensor rate).
+constexpr uint32_t kBiasBits = 0x4B400000u;
+constexpr float kBiasF = 12582912.0f;
+// The epilogue accumulates s_g * (kBiasF + 16P_g) and removes the accumulated bias
+// sum every kBiasFlush groups: 1 + 1/kBiasFlush fp32 operations per element and
+// group, with the running value never more than kBiasFlush biased terms away from the
+// result (rounding error ~2^-9 of a typical partial's scale, far below a bf16 ulp).
+constexpr uint32_t kBiasFlush = 4;
 
 struct Params {
   CUtensorMap tm_tok;  // A  [M][K] u8 view of int8, box {128, BT}, SW128
@@ -70,7 +84,7 @@ template <uint32_t BT, uint32_t EWG, uint32_t LS>
 struct Cfg {
   static_assert(BT == 16 || BT == 32 || BT == 64 || BT == 128, "token tile");
   static_assert(EWG == 1 || EWG == 2, "epilogue warpgroups");
-  static constexpr uint32_t kLoadStages = LS;
+  static constexpr uint32_t kStages = LS;
   static constexpr uint32_t kThreads = 256 + 128 * EWG;
   static constexpr uint32_t kCols = BT / EWG;               // columns per epilogue thread
   static constexpr uint32_t kChunk = kCols < 32 ? kCols : 32;
@@ -78,20 +92,23 @@ struct Cfg {
   static constexpr uint32_t kTokBytes = BT * kGroupK;
   static constexpr uint32_t kWpBytes = kRows * kPackedRow;
   static constexpr uint32_t kWBytes = kRows * kGroupK;
+  static_assert(kCols % 8 == 0 && kChunk % 2 == 0, "epilogue column split");
 };
 
+// One ring of LS stages; stage s holds the token tile, the packed weight tile and
+// its unpacked int8 copy of the same K-group, so a single UMMA commit per group
+// (`consumed`) frees all three.
 template <uint32_t BT, uint32_t EWG, uint32_t LS>
 struct alignas(1024) Smem {
   using C = Cfg<BT, EWG, LS>;
-  uint8_t w[kUnpackStages][C::kWBytes];         // unpacked int8, SW128 (UMMA A)
+  uint8_t w[LS][C::kWBytes];                    // unpacked int8, SW128 (UMMA A)
   uint8_t tok[LS][C::kTokBytes];                // tokens, SW128 (UMMA B)
   uint8_t wp[LS][C::kWpBytes];                  // packed int4 straight from TMA
   uint8_t out[BT * kRows * 2];                  // output staging [BT][128] bf16
   float sa[BT];
-  uint64_t load_full[LS];
-  uint64_t load_empty[LS];
-  uint64_t unpack_full[kUnpackStages];
-  uint64_t unpack_empty[kUnpackStages];
+  uint64_t load_full[LS];                       // TMA bytes landed (tokens + packed W)
+  uint64_t unpack_full[LS];                     // 4 unpack warps wrote w[s]
+  uint64_t consumed[LS];                        // UMMAs of stage s finished reading it
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
   uint64_t drain;
@@ -163,11 +180,8 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
     tma_prefetch_desc(&p.tm_out);
     for (uint32_t i = 0; i < LS; ++i) {
       mbar_init(&s.load_full[i], 1);
-      mbar_init(&s.load_empty[i], 2);  // MMA commit (tokens) + unpack warpgroup (packed W)
-    }
-    for (uint32_t i = 0; i < kUnpackStages; ++i) {
       mbar_init(&s.unpack_full[i], 4);  // one arrive per unpack warp
-      mbar_init(&s.unpack_empty[i], 1);
+      mbar_init(&s.consumed[i], 1);     // UMMA commit
     }
     for (uint32_t i = 0; i < 2; ++i) {
       mbar_init(&s.tmem_full[i], 1);
@@ -184,10 +198,24 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
+  const uint32_t tmem_base = s.tmem_base;
+  if (warp >= 8) {
+    // Arm both accumulators with the bias before the first UMMA may touch them.
+    const uint32_t ew = warp - 8;
+    const uint32_t row = tmem_base + (((ew & 3u) * 32u) << 16) + (ew >> 2) * C::kCols;
+#pragma unroll
+    for (uint32_t b = 0; b < 2; ++b) {
+#pragma unroll
+      for (uint32_t c = 0; c < C::kCols; c += 8) tmem_st_32x32b_x8_fill(row + b * BT + c, kBiasBits);
+    }
+    tmem_st_wait();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
   // The prologue above may overlap the previous grid in the stream (programmatic
   // dependent launch); global memory is only touched after it has completed.
   pdl_wait();
-  const uint32_t tmem_base = s.tmem_base;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -198,7 +226,7 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
       bool ok = true;
       while (ok && next_work<BT>(p, cursor, w)) {
         for (uint32_t g = w.g_begin; g < w.g_end; ++g) {
-          if (!mbar_wait(&s.load_empty[stage], phase ^ 1u, abort, kStatusTimeoutProducer)) {
+          if (!mbar_wait(&s.consumed[stage], phase ^ 1u, abort, kStatusTimeoutProducer)) {
             ok = false;
             break;
           }
@@ -223,7 +251,7 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
     // ------------------------------------------------------------ UMMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_s8_s32(kRows, BT);
-      uint32_t stage = 0, phase = 0, ustage = 0, uphase = 0, gi = 0, cursor = 0;
+      uint32_t stage = 0, phase = 0, gi = 0, cursor = 0;
       Work w;
       bool ok = true;
       while (ok && next_work<BT>(p, cursor, w)) {
@@ -231,30 +259,26 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
           const uint32_t acc = gi & 1u;
           const uint32_t acc_phase = (gi >> 1) & 1u;
           if (!mbar_wait(&s.tmem_empty[acc], acc_phase ^ 1u, abort, kStatusTimeoutMma) ||
-              !mbar_wait(&s.unpack_full[ustage], uphase, abort, kStatusTimeoutMma) ||
+              !mbar_wait(&s.unpack_full[stage], phase, abort, kStatusTimeoutMma) ||
               !mbar_wait(&s.load_full[stage], phase, abort, kStatusTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after_sync();
-          const uint64_t adesc = make_sw128_kmajor_desc(s.w[ustage]);
+          const uint64_t adesc = make_sw128_kmajor_desc(s.w[stage]);
           const uint64_t bdesc = make_sw128_kmajor_desc(s.tok[stage]);
           const uint32_t d_tmem = tmem_base + acc * BT;
+          // Every UMMA accumulates: the group starts from the bias the epilogue left.
 #pragma unroll
           for (uint32_t k = 0; k < kGroupK / kUmmaK; ++k) {
             umma_s8(d_tmem, desc_advance(adesc, k * kUmmaK), desc_advance(bdesc, k * kUmmaK), idesc,
-                    k != 0u ? 1u : 0u);
+                    1u);
           }
-          umma_commit(&s.load_empty[stage]);
-          umma_commit(&s.unpack_empty[ustage]);
+          umma_commit(&s.consumed[stage]);
           umma_commit(&s.tmem_full[acc]);
           if (++stage == LS) {
             stage = 0;
             phase ^= 1u;
-          }
-          if (++ustage == kUnpackStages) {
-            ustage = 0;
-            uphase ^= 1u;
           }
         }
       }
@@ -264,15 +288,15 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------ unpack warpgroup
     const uint32_t ut = threadIdx.x - 128;  // 0..127
-    uint32_t stage = 0, phase = 0, ustage = 0, uphase = 0, cursor = 0;
+    uint32_t stage = 0, phase = 0, cursor = 0;
     Work w;
     bool ok = true;
     while (ok && next_work<BT>(p, cursor, w)) {
       for (uint32_t g = w.g_begin; g < w.g_end; ++g) {
         if (ut == 0) {
+          // Packed tile landed, and the UMMAs that read w[stage] last time are done.
           s.unpack_ok = (mbar_wait(&s.load_full[stage], phase, abort, kStatusTimeoutUnpack) &&
-                         mbar_wait(&s.unpack_empty[ustage], uphase ^ 1u, abort,
-                                   kStatusTimeoutUnpack))
+                         mbar_wait(&s.consumed[stage], phase ^ 1u, abort, kStatusTimeoutUnpack))
                             ? 1u
                             : 0u;
         }
@@ -282,7 +306,7 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
           break;
         }
         const uint8_t* src = s.wp[stage];
-        uint8_t* dst = s.w[ustage];
+        uint8_t* dst = s.w[stage];
         // 1024 chunks of 8 packed bytes -> 16 int8; thread ut handles chunk id = i*128+ut.
         // Reads: a warp covers 256 contiguous bytes. Writes: the 8 threads of a
         // quarter-warp fill one 128-byte swizzled row.
@@ -298,17 +322,12 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&s.unpack_full[ustage]);
-        // All four warps have read s.wp[stage]; only then may the producer refill it.
-        named_barrier_sync(2, 128);
-        if (ut == 0) mbar_arrive(&s.load_empty[stage]);
+        // The warp's reads of wp[stage] are complete here, so this arrival (through
+        // the UMMA commit on `consumed`) is also what lets the producer refill it.
+        if (lane == 0) mbar_arrive(&s.unpack_full[stage]);
         if (++stage == LS) {
           stage = 0;
           phase ^= 1u;
-        }
-        if (++ustage == kUnpackStages) {
-          ustage = 0;
-          uphase ^= 1u;
         }
       }
     }
@@ -321,15 +340,17 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
     const uint32_t nl = q * 32 + lane;       // weight row (output column) within the tile
     const uint32_t col0 = h * C::kCols;      // first token column of this thread
     const uint32_t n_epi = 128 * EWG;
+    constexpr uint32_t kPairs = C::kCols / 2;
     uint32_t gi = 0, cursor = 0;
     Work w;
     bool ok = true;
     while (ok && next_work<BT>(p, cursor, w)) {
       const uint32_t n = w.n0 + nl;
       const bool n_valid = (nl < p.R) && (n < p.N);
-      float acc[C::kCols];
+      uint64_t acc[kPairs];
 #pragma unroll
-      for (uint32_t j = 0; j < C::kCols; ++j) acc[j] = 0.f;
+      for (uint32_t j = 0; j < kPairs; ++j) acc[j] = 0ull;
+      float bias_sum = 0.f;
 
       // Weight scale of the first group, then one group ahead.
       float s_next = 0.f;
@@ -341,6 +362,7 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
         if (n_valid && g + 1 < w.g_end) {
           s_next = bf16_bits_to_float(__ldg(p.sb + size_t(n) * p.ldsb + g + 1));
         }
+        const uint64_t s2 = f32x2_pack(s_g, s_g);
         const uint32_t acc_b = gi & 1u;
         const uint32_t acc_phase = (gi >> 1) & 1u;
         if (et == 0) {
@@ -364,24 +386,37 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
           }
           tmem_ld_wait();
           if (c0 + C::kChunk == C::kCols) {
+            // Every column of this thread has been read: re-arm the bias, then hand
+            // the accumulator back to the UMMA issuer.
+#pragma unroll
+            for (uint32_t c = 0; c < C::kCols; c += 8) tmem_st_32x32b_x8_fill(t_row + c, kBiasBits);
+            tmem_st_wait();
             tc_fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s.tmem_empty[acc_b]);
           }
 #pragma unroll
-          for (uint32_t j = 0; j < C::kChunk; ++j) {
-            const int32_t v = static_cast<int32_t>(r[j]);
-            acc[c0 + j] = fmaf(static_cast<float>(v), s_g, acc[c0 + j]);
+          for (uint32_t j = 0; j < C::kChunk; j += 2) {
+            acc[(c0 + j) / 2] = f32x2_fma(f32x2_pack(__uint_as_float(r[j]), __uint_as_float(r[j + 1])),
+                                          s2, acc[(c0 + j) / 2]);
           }
           if (p.partials != nullptr && n_valid) {
 #pragma unroll
             for (uint32_t j = 0; j < C::kChunk; ++j) {
               const uint32_t m = w.m0 + col0 + c0 + j;
               if (m < p.M) {
-                p.partials[(size_t(m) * p.N + n) * p.G + g] = static_cast<int32_t>(r[j]) >> 4;
+                p.partials[(size_t(m) * p.N + n) * p.G + g] =
+                    static_cast<int32_t>(r[j] - kBiasBits) >> 4;
               }
             }
           }
+        }
+        bias_sum += s_g * kBiasF;  // exact: 8 significant bits times 2
+        if ((g - w.g_begin) % kBiasFlush == kBiasFlush - 1u || g + 1 == w.g_end) {
+          const uint64_t nb = f32x2_pack(-bias_sum, -bias_sum);
+#pragma unroll
+          for (uint32_t j = 0; j < kPairs; ++j) acc[j] = f32x2_add(acc[j], nb);
+          bias_sum = 0.f;
         }
       }
       if (!ok) break;
@@ -393,9 +428,13 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
         named_barrier_sync(1, n_epi);
         uint16_t* o = reinterpret_cast<uint16_t*>(s.out);
 #pragma unroll
-        for (uint32_t j = 0; j < C::kCols; ++j) {
-          const float v = acc[j] * s.sa[col0 + j];
-          o[(col0 + j) * kRows + nl] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+        for (uint32_t j = 0; j < kPairs; ++j) {
+          float a0, a1;
+          f32x2_unpack(acc[j], a0, a1);
+          o[(col0 + 2 * j) * kRows + nl] =
+              __bfloat16_as_ushort(__float2bfloat16_rn(a0 * s.sa[col0 + 2 * j]));
+          o[(col0 + 2 * j + 1) * kRows + nl] =
+              __bfloat16_as_ushort(__float2bfloat16_rn(a1 * s.sa[col0 + 2 * j + 1]));
         }
         fence_proxy_async_smem();
         named_barrier_sync(1, n_epi);

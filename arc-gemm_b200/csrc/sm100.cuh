@@ -358,6 +358,20 @@ __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Registers -> TMEM: the same 32-bit value into 8 consecutive columns of this
+// thread's lane (same lane-quarter rule as the loads).
+__device__ __forceinline__ void tmem_st_32x32b_x8_fill(uint32_t taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};"
+      :
+      : "r"(taddr), "r"(v)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // ---------------------------------------------------------------------------------
 // UMMA descriptors
 // ---------------------------------------------------------------------------------
@@ -461,6 +475,30 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 
 __device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
   return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+
+// Packed fp32 pair arithmetic (sm_100): one instruction for two lanes of work.
+__device__ __forceinline__ uint64_t f32x2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ void f32x2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+// acc = x * s + acc, elementwise on pairs, round to nearest even.
+__device__ __forceinline__ uint64_t f32x2_fma(uint64_t x, uint64_t s, uint64_t acc) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(x), "l"(s), "l"(acc));
+  return r;
+}
+
+__device__ __forceinline__ uint64_t f32x2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
 }
 
 }  // namespace arcb
