@@ -132,8 +132,8 @@ constexpr size_t decode_smem_bytes() {
 
 // The persistent-tile instantiations the dispatcher can pick (M > 32).
 #define ARC_A8W4_VARIANTS(X) \
-  X(64, 1, 5)                \
-  X(128, 2, 4)
+  X(64, 1, 8)                \
+  X(128, 2, 7)
 
 int init_device(int dev) {
   DeviceState& st = g_dev[dev];
@@ -151,13 +151,30 @@ int init_device(int dev) {
     }
     st.sms = prop.multiProcessorCount;
     e = allow_smem(arcb::bf16::gemm_bf16_kernel, arcb::bf16::kSmemBytes);
+    // The persistent kernel moves registers between its warpgroups (setmaxnreg); the
+    // shares are sized for a launch count of Cfg::kLaunchRegs per thread, and a
+    // different compiled count could leave an increase waiting, so refuse it.
+    bool regs_ok = true;
 #define ARC_SET_ATTR(BT, EWG, LS)                                                     \
   if (e == cudaSuccess) {                                                             \
     e = allow_smem(arcb::a8w4::gemm_a8w4_kernel<BT, EWG, LS>,                         \
                    a8w4_smem_bytes<BT, EWG, LS>());                                   \
+  }                                                                                   \
+  if (e == cudaSuccess) {                                                             \
+    cudaFuncAttributes fa;                                                            \
+    e = cudaFuncGetAttributes(&fa, arcb::a8w4::gemm_a8w4_kernel<BT, EWG, LS>);        \
+    if (e == cudaSuccess &&                                                           \
+        fa.numRegs != static_cast<int>(arcb::a8w4::Cfg<BT, EWG, LS>::kLaunchRegs)) {  \
+      regs_ok = false;                                                                \
+    }                                                                                 \
   }
     ARC_A8W4_VARIANTS(ARC_SET_ATTR)
 #undef ARC_SET_ATTR
+    if (e == cudaSuccess && !regs_ok) {
+      st.status = fail(ARC_ERR_UNSUPPORTED,
+                       "gemm_a8w4_kernel was compiled with an unexpected register count");
+      return;
+    }
     if (e == cudaSuccess) {
       e = allow_smem(arcb::a8w4dec::gemm_a8w4_decode_kernel<16>, decode_smem_bytes<16>());
     }
@@ -302,7 +319,7 @@ int plan_a8w4(int M, int N, int K, int sms, int max_c2, int max_c4, arc_a8w4_pla
   plan->weight_rows = static_cast<int>(arcb::a8w4::kRows);
   plan->k_split = 1;
   plan->grid = static_cast<int>(tiles < static_cast<uint32_t>(sms) ? tiles : sms);
-  plan->load_stages = bt == 64 ? 5 : 4;
+  plan->load_stages = bt == 64 ? 8 : 7;
   plan->groups_per_stage = 1;
   return ARC_OK;
 }
@@ -540,10 +557,6 @@ int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uin
                          Q::kPackedRow, R, CU_TENSOR_MAP_SWIZZLE_NONE, "Wp")) {
     return st;
   }
-  if (int st = encode_2d(&p.tm_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, N, M, N, Q::kRows, BT,
-                         CU_TENSOR_MAP_SWIZZLE_NONE, "C")) {
-    return st;
-  }
   p.sa = sa;
   p.sb = sb;
   p.out = C;
@@ -560,11 +573,11 @@ int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uin
   p.num_tiles = p.tiles_m * p.tiles_n;
   const uint32_t grid = static_cast<uint32_t>(plan.grid);
   if (BT == 64) {
-    e = launch_ex(Q::gemm_a8w4_kernel<64, 1, 5>, p, grid, Q::Cfg<64, 1, 5>::kThreads,
-                  a8w4_smem_bytes<64, 1, 5>(), 1, stream);
+    e = launch_ex(Q::gemm_a8w4_kernel<64, 1, 8>, p, grid, Q::Cfg<64, 1, 8>::kThreads,
+                  a8w4_smem_bytes<64, 1, 8>(), 1, stream);
   } else {
-    e = launch_ex(Q::gemm_a8w4_kernel<128, 2, 4>, p, grid, Q::Cfg<128, 2, 4>::kThreads,
-                  a8w4_smem_bytes<128, 2, 4>(), 1, stream);
+    e = launch_ex(Q::gemm_a8w4_kernel<128, 2, 7>, p, grid, Q::Cfg<128, 2, 7>::kThreads,
+                  a8w4_smem_bytes<128, 2, 7>(), 1, stream);
   }
   if (e != cudaSuccess) return cuda_fail(e, "gemm_a8w4_kernel launch");
   return ARC_OK;

@@ -27,19 +27,26 @@
 //
 // Roles (256 + 128*EWG threads):
 //   warp 0        TMA producer: token tile [BT x 128 B] (SW128) + packed weight tile
-//                 [R x 64 B] per K-group into stage s of an LS-stage ring
+//                 [128 x 64 B] per K-group into an LS-stage load ring
 //   warp 1        UMMA issuer: 4 x tcgen05.mma kind::i8 M=128 N=BT K=32 per group into
-//                 one of two TMEM accumulators (a fresh int32 partial per group, on
-//                 top of the bias described at kBiasBits); two commits per group
+//                 one of kAcc TMEM accumulators (a fresh int32 partial per group, on
+//                 top of the bias described at kBiasBits), then ONE commit per group
 //   warp 2        TMEM allocator
 //   warp 3        idle
-//   warps 4-7     unpack warpgroup: packed smem -> int8 SW128 smem in the same stage
+//   warps 4-7     unpack warpgroup: packed smem -> int8 SW128 smem (kUnpacked-stage ring)
 //   warps 8-...   epilogue warpgroup(s): tcgen05.ld partial, re-arm the bias, fp32
-//                 scale-accumulate on packed f32x2 pairs
+//                 scale-accumulate on packed f32x2 pairs, bf16 stores to global
+//
+// Synchronisation: the single per-group commit lands on mma_done[gi % 8] (gi counts
+// the CTA's groups). It tells the producer that load stage gi % LS is free again
+// (waited LS groups later), the unpack warps that unpacked stage gi % kUnpacked is
+// free (kUnpacked groups later) and the epilogue that accumulator gi % kAcc holds
+// group gi. Each waiter is at most one phase behind the barrier it tests, which the
+// bounds LS, kUnpacked <= 8 and kAcc < 8 guarantee.
 //
 // Work decomposition: persistent CTAs stride over (token tile, weight tile) pairs;
-// each tile covers all K-groups and is stored through TMA. Decode-sized M (<= 32)
-// uses the dedicated kernel in gemm_a8w4_decode.cuh instead.
+// each tile covers all K-groups. Decode-sized M (<= 32) uses the dedicated kernel in
+// gemm_a8w4_decode.cuh instead.
 #pragma once
 
 #include "sm100.cuh"
@@ -51,12 +58,15 @@ constexpr uint32_t kRows = 128;        // UMMA M: weight rows per tile (TMEM lan
 constexpr uint32_t kGroupK = 128;      // K elements per scale group = one 128-byte row
 constexpr uint32_t kPackedRow = 64;    // bytes of packed int4 per row per group
 constexpr uint32_t kUmmaK = 32;        // K per kind::i8 UMMA (32 bytes)
+constexpr uint32_t kUnpacked = 3;      // unpacked weight stages
+constexpr uint32_t kAcc = 4;           // TMEM accumulators
+constexpr uint32_t kDoneRing = 8;      // per-group completion barriers
+
 // Accumulator bias. Between uses every int32 accumulator column in TMEM holds
 // kBiasBits, the bit pattern of kBiasF = 1.5 * 2^23, and the UMMAs of a K-group
 // accumulate onto it. Since |16 P| < 2^22, the int32 sum kBiasBits + 16P is exactly
 // the bit pattern of the float kBiasF + 16P, so a partial is read back as a float with
-// no int->float conversion instruction (those issue on a quarter-rate pipe and would
-// cap the kernel far below the tensor rate).
+// no int->float conversion instruction.
 constexpr uint32_t kBiasBits = 0x4B400000u;
 constexpr float kBiasF = 12582912.0f;
 // The epilogue accumulates s_g * (kBiasF + 16P_g) and removes the accumulated bias
@@ -67,8 +77,7 @@ constexpr uint32_t kBiasFlush = 4;
 
 struct Params {
   CUtensorMap tm_tok;  // A  [M][K] u8 view of int8, box {128, BT}, SW128
-  CUtensorMap tm_wp;   // Wp [N][K/2] u8, box {64, R}, no swizzle
-  CUtensorMap tm_out;  // out [M][N] bf16, box {128, BT}, no swizzle
+  CUtensorMap tm_wp;   // Wp [N][K/2] u8, box {64, 128}, no swizzle
   const float* sa;
   const uint16_t* sb;
   uint16_t* out;
@@ -76,47 +85,51 @@ struct Params {
   uint32_t M, N, K, G;
   uint32_t ldsb;       // elements between sb rows
   uint32_t ldc;        // elements between out rows
-  uint32_t R;          // valid weight rows per tile (multiple of 8, <= 128)
+  uint32_t R;          // weight rows per tile (128)
   uint32_t tiles_m, tiles_n, num_tiles;
 };
 
 template <uint32_t BT, uint32_t EWG, uint32_t LS>
 struct Cfg {
-  static_assert(BT == 16 || BT == 32 || BT == 64 || BT == 128, "token tile");
+  static_assert(BT == 64 || BT == 128, "token tile");
   static_assert(EWG == 1 || EWG == 2, "epilogue warpgroups");
-  static constexpr uint32_t kStages = LS;
+  static_assert(LS >= 2 && LS <= kDoneRing && kUnpacked <= kDoneRing && kAcc < kDoneRing,
+                "each waiter must stay within one phase of its completion barrier");
   static constexpr uint32_t kThreads = 256 + 128 * EWG;
   static constexpr uint32_t kCols = BT / EWG;               // columns per epilogue thread
-  static constexpr uint32_t kChunk = kCols < 32 ? kCols : 32;
-  static constexpr uint32_t kTmemCols = (2 * BT) < 32 ? 32 : 2 * BT;
+  static constexpr uint32_t kChunk = 32;                    // TMEM columns per load
+  // Register budget: the producer/UMMA and unpack warpgroups drop to kRegsLow and
+  // the epilogue warpgroup(s) rise to kRegsHigh, out of kLaunchRegs per thread at
+  // launch (the most 1 CTA/SM allows; the host checks the compiled count).
+  static constexpr uint32_t kLaunchRegs = EWG == 2 ? 128 : 168;
+  static constexpr bool kSplitRegs = true;
+  static constexpr uint32_t kRegsLow = EWG == 2 ? 80 : 112;
+  static constexpr uint32_t kRegsHigh = EWG == 2 ? 176 : 232;
+  static_assert(256 * kRegsLow + 128 * EWG * kRegsHigh <= kThreads * kLaunchRegs,
+                "register shares exceed the launch budget");
+  static constexpr uint32_t kTmemCols = kAcc * BT;          // 256 or 512
   static constexpr uint32_t kTokBytes = BT * kGroupK;
   static constexpr uint32_t kWpBytes = kRows * kPackedRow;
   static constexpr uint32_t kWBytes = kRows * kGroupK;
-  static_assert(kCols % 8 == 0 && kChunk % 2 == 0, "epilogue column split");
+  static_assert(kCols % kChunk == 0, "epilogue column split");
 };
 
-// One ring of LS stages; stage s holds the token tile, the packed weight tile and
-// its unpacked int8 copy of the same K-group, so a single UMMA commit per group
-// (`consumed`) frees all three.
 template <uint32_t BT, uint32_t EWG, uint32_t LS>
 struct alignas(1024) Smem {
   using C = Cfg<BT, EWG, LS>;
-  uint8_t w[LS][C::kWBytes];                    // unpacked int8, SW128 (UMMA A)
+  uint8_t w[kUnpacked][C::kWBytes];             // unpacked int8, SW128 (UMMA A)
   uint8_t tok[LS][C::kTokBytes];                // tokens, SW128 (UMMA B)
   uint8_t wp[LS][C::kWpBytes];                  // packed int4 straight from TMA
-  uint8_t out[BT * kRows * 2];                  // output staging [BT][128] bf16
-  float sa[BT];
   uint64_t load_full[LS];                       // TMA bytes landed (tokens + packed W)
-  uint64_t unpack_full[LS];                     // 4 unpack warps wrote w[s]
-  uint64_t consumed[LS];                        // UMMAs of stage s finished reading it
-  uint64_t tmem_full[2];
-  uint64_t tmem_empty[2];
-  uint64_t drain;
+  uint64_t w_full[kUnpacked];                   // 4 unpack warps wrote w[u]
+  uint64_t mma_done[kDoneRing];                 // the UMMAs of group gi retired
+  uint64_t tmem_empty[kAcc];                    // epilogue read accumulator a
   uint32_t tmem_base;
   uint32_t abort;
-  uint32_t unpack_ok;
-  uint32_t epi_ok;
 };
+
+// Parity of the completion of mma_done that belongs to group gi.
+__device__ __forceinline__ uint32_t done_parity(uint32_t gi) { return (gi / kDoneRing) & 1u; }
 
 // ---------------------------------------------------------------------------------
 // Work decomposition
@@ -173,21 +186,19 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
   const uint32_t lane = threadIdx.x & 31u;
   volatile uint32_t* abort = &s.abort;
 
+  // Probe stamps (probe build only): steady-state groups 8..15 of the first tile.
+  //   0-7 UMMA waits passed   8-15 partial seen by the epilogue   16-23 accumulator
+  //   released   24-31 unpack waits passed   32-39 stage unpacked   40-47 loads
+  //   issued   48-55 group accumulated   56 entry   57 prologue done   59 exit
+  if (threadIdx.x == 0) probe_mark(56);
   pdl_launch_dependents();
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&p.tm_tok);
     tma_prefetch_desc(&p.tm_wp);
-    tma_prefetch_desc(&p.tm_out);
-    for (uint32_t i = 0; i < LS; ++i) {
-      mbar_init(&s.load_full[i], 1);
-      mbar_init(&s.unpack_full[i], 4);  // one arrive per unpack warp
-      mbar_init(&s.consumed[i], 1);     // UMMA commit
-    }
-    for (uint32_t i = 0; i < 2; ++i) {
-      mbar_init(&s.tmem_full[i], 1);
-      mbar_init(&s.tmem_empty[i], 4 * EWG);
-    }
-    mbar_init(&s.drain, 1);
+    for (uint32_t i = 0; i < LS; ++i) mbar_init(&s.load_full[i], 1);
+    for (uint32_t i = 0; i < kUnpacked; ++i) mbar_init(&s.w_full[i], 4);  // one per unpack warp
+    for (uint32_t i = 0; i < kDoneRing; ++i) mbar_init(&s.mma_done[i], 1);  // UMMA commit
+    for (uint32_t i = 0; i < kAcc; ++i) mbar_init(&s.tmem_empty[i], 4 * EWG);
     s.abort = 0;
     fence_barrier_init();
   }
@@ -200,11 +211,11 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
   tc_fence_after_sync();
   const uint32_t tmem_base = s.tmem_base;
   if (warp >= 8) {
-    // Arm both accumulators with the bias before the first UMMA may touch them.
+    // Arm every accumulator with the bias before the first UMMA may touch it.
     const uint32_t ew = warp - 8;
     const uint32_t row = tmem_base + (((ew & 3u) * 32u) << 16) + (ew >> 2) * C::kCols;
 #pragma unroll
-    for (uint32_t b = 0; b < 2; ++b) {
+    for (uint32_t b = 0; b < kAcc; ++b) {
 #pragma unroll
       for (uint32_t c = 0; c < C::kCols; c += 8) tmem_st_32x32b_x8_fill(row + b * BT + c, kBiasBits);
     }
@@ -216,56 +227,65 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
   // The prologue above may overlap the previous grid in the stream (programmatic
   // dependent launch); global memory is only touched after it has completed.
   pdl_wait();
-
+  if (threadIdx.x == 0) probe_mark(57);
+  // Register moves sit inside each role's branch, so that the compiler gives every
+  // role's code the budget of that role.
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
+    if constexpr (C::kSplitRegs) regs_release<C::kRegsLow>();
     if (lane == 0) {
-      uint32_t stage = 0, phase = 0, issued = 0, cursor = 0;
-      const uint32_t tx = C::kTokBytes + p.R * kPackedRow;
+      uint32_t stage = 0, phase = 0, gi = 0, cursor = 0;
+      const uint32_t tx = C::kTokBytes + C::kWpBytes;
       Work w;
       bool ok = true;
       while (ok && next_work<BT>(p, cursor, w)) {
-        for (uint32_t g = w.g_begin; g < w.g_end; ++g) {
-          if (!mbar_wait(&s.consumed[stage], phase ^ 1u, abort, kStatusTimeoutProducer)) {
+        for (uint32_t g = w.g_begin; g < w.g_end; ++g, ++gi) {
+          // Stage `stage` last served group gi - LS; its UMMAs (which ran after the
+          // unpack warps had read the packed half) must have retired.
+          if (gi >= LS && !mbar_wait(&s.mma_done[(gi - LS) % kDoneRing], done_parity(gi - LS),
+                                     abort, kStatusTimeoutProducer)) {
             ok = false;
             break;
           }
+          if (gi - 8u < 8u) probe_mark(40 + gi - 8u);
           mbar_arrive_expect_tx(&s.load_full[stage], tx);
           tma_load_2d(&p.tm_tok, &s.load_full[stage], s.tok[stage], int32_t(g * kGroupK),
                       int32_t(w.m0), kCacheEvictLast);
           tma_load_2d(&p.tm_wp, &s.load_full[stage], s.wp[stage], int32_t(g * kPackedRow),
                       int32_t(w.n0), kCacheEvictFirst);
-          ++issued;
           if (++stage == LS) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
-      const uint32_t n_drain = issued < LS ? issued : LS;
-      for (uint32_t i = issued - n_drain; i < issued; ++i) {
+      // Let the loads still in flight land before the CTA may exit.
+      const uint32_t n_drain = gi < LS ? gi : LS;
+      for (uint32_t i = gi - n_drain; i < gi; ++i) {
         mbar_drain(&s.load_full[i % LS], (i / LS) & 1u);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ UMMA issuer
+    if constexpr (C::kSplitRegs) regs_release<C::kRegsLow>();
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_s8_s32(kRows, BT);
-      uint32_t stage = 0, phase = 0, gi = 0, cursor = 0;
+      uint32_t stage = 0, phase = 0, us = 0, uphase = 0, gi = 0, cursor = 0;
       Work w;
       bool ok = true;
       while (ok && next_work<BT>(p, cursor, w)) {
         for (uint32_t g = w.g_begin; g < w.g_end; ++g, ++gi) {
-          const uint32_t acc = gi & 1u;
-          const uint32_t acc_phase = (gi >> 1) & 1u;
-          if (!mbar_wait(&s.tmem_empty[acc], acc_phase ^ 1u, abort, kStatusTimeoutMma) ||
-              !mbar_wait(&s.unpack_full[stage], phase, abort, kStatusTimeoutMma) ||
+          const uint32_t acc = gi % kAcc;
+          if ((gi >= kAcc && !mbar_wait(&s.tmem_empty[acc], (gi / kAcc - 1u) & 1u, abort,
+                                        kStatusTimeoutMma)) ||
+              !mbar_wait(&s.w_full[us], uphase, abort, kStatusTimeoutMma) ||
               !mbar_wait(&s.load_full[stage], phase, abort, kStatusTimeoutMma)) {
             ok = false;
             break;
           }
+          if (gi - 8u < 8u) probe_mark(gi - 8u);
           tc_fence_after_sync();
-          const uint64_t adesc = make_sw128_kmajor_desc(s.w[stage]);
+          const uint64_t adesc = make_sw128_kmajor_desc(s.w[us]);
           const uint64_t bdesc = make_sw128_kmajor_desc(s.tok[stage]);
           const uint32_t d_tmem = tmem_base + acc * BT;
           // Every UMMA accumulates: the group starts from the bias the epilogue left.
@@ -274,73 +294,88 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
             umma_s8(d_tmem, desc_advance(adesc, k * kUmmaK), desc_advance(bdesc, k * kUmmaK), idesc,
                     1u);
           }
-          umma_commit(&s.consumed[stage]);
-          umma_commit(&s.tmem_full[acc]);
+          umma_commit(&s.mma_done[gi % kDoneRing]);
           if (++stage == LS) {
             stage = 0;
             phase ^= 1u;
           }
+          if (++us == kUnpacked) {
+            us = 0;
+            uphase ^= 1u;
+          }
         }
       }
-      umma_commit(&s.drain);
-      mbar_drain(&s.drain, 0);
+      // The last commit covers every UMMA this thread issued.
+      if (gi > 0u) mbar_drain(&s.mma_done[(gi - 1u) % kDoneRing], done_parity(gi - 1u));
     }
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------ unpack warpgroup
+    if constexpr (C::kSplitRegs) regs_release<C::kRegsLow>();
     const uint32_t ut = threadIdx.x - 128;  // 0..127
-    uint32_t stage = 0, phase = 0, cursor = 0;
+    uint32_t stage = 0, phase = 0, us = 0, gi = 0, cursor = 0;
+    // Each warp waits for itself (no warpgroup barrier per group).
+    // Thread ut converts 16-byte chunks id = i*128 + ut (i < 4) of the 8 KB packed
+    // tile: row r = id / 4, packed bytes [16c, 16c+16) with c = id % 4, which become
+    // the 32 int8 bytes [32c, 32c+32) of row r = swizzled 16-byte chunks 2c and 2c+1.
+    // Reads: a warp covers 512 contiguous bytes. Writes: a quarter-warp covers two
+    // rows whose chunk sets {2c ^ (r&7)} are the even and the odd chunks: no conflicts.
+    const uint32_t c16 = ut & 3u;
     Work w;
     bool ok = true;
     while (ok && next_work<BT>(p, cursor, w)) {
-      for (uint32_t g = w.g_begin; g < w.g_end; ++g) {
-        if (ut == 0) {
-          // Packed tile landed, and the UMMAs that read w[stage] last time are done.
-          s.unpack_ok = (mbar_wait(&s.load_full[stage], phase, abort, kStatusTimeoutUnpack) &&
-                         mbar_wait(&s.consumed[stage], phase ^ 1u, abort, kStatusTimeoutUnpack))
-                            ? 1u
-                            : 0u;
-        }
-        named_barrier_sync(2, 128);
-        if (*reinterpret_cast<volatile uint32_t*>(&s.unpack_ok) == 0u) {
+      for (uint32_t g = w.g_begin; g < w.g_end; ++g, ++gi) {
+        // Packed tile landed, and the UMMAs that read w[us] last time have retired.
+        if (!mbar_wait_warp(&s.load_full[stage], phase, abort, kStatusTimeoutUnpack) ||
+            (gi >= kUnpacked &&
+             !mbar_wait_warp(&s.mma_done[(gi - kUnpacked) % kDoneRing], done_parity(gi - kUnpacked),
+                             abort, kStatusTimeoutUnpack))) {
           ok = false;
           break;
         }
+        if (ut == 0 && gi - 8u < 8u) probe_mark(24 + gi - 8u);
         const uint8_t* src = s.wp[stage];
-        uint8_t* dst = s.w[stage];
-        // 1024 chunks of 8 packed bytes -> 16 int8; thread ut handles chunk id = i*128+ut.
-        // Reads: a warp covers 256 contiguous bytes. Writes: the 8 threads of a
-        // quarter-warp fill one 128-byte swizzled row.
+        uint8_t* dst = s.w[us];
+        uint4 x[4];
 #pragma unroll
-        for (uint32_t i = 0; i < 8; ++i) {
-          const uint32_t id = i * 128u + ut;
-          const uint32_t r = id >> 3, c = id & 7u;
-          const uint2 x = *reinterpret_cast<const uint2*>(src + r * kPackedRow + c * 8u);
-          const uint2 lo = expand_int4x8(x.x);
-          const uint2 hi = expand_int4x8(x.y);
-          *reinterpret_cast<uint4*>(dst + r * kGroupK + (((c ^ (r & 7u)) << 4))) =
-              make_uint4(lo.x, lo.y, hi.x, hi.y);
+        for (uint32_t i = 0; i < 4; ++i) {
+          x[i] = *reinterpret_cast<const uint4*>(src + (i * 128u + ut) * 16u);
+        }
+#pragma unroll
+        for (uint32_t i = 0; i < 4; ++i) {
+          const uint32_t r = (i * 128u + ut) >> 2;
+          const uint2 a = expand_int4x8(x[i].x), b = expand_int4x8(x[i].y);
+          const uint2 c = expand_int4x8(x[i].z), d = expand_int4x8(x[i].w);
+          uint8_t* row = dst + r * kGroupK;
+          *reinterpret_cast<uint4*>(row + (((2u * c16) ^ (r & 7u)) << 4)) = make_uint4(a.x, a.y, b.x, b.y);
+          *reinterpret_cast<uint4*>(row + (((2u * c16 + 1u) ^ (r & 7u)) << 4)) =
+              make_uint4(c.x, c.y, d.x, d.y);
         }
         fence_proxy_async_smem();
         __syncwarp();
-        // The warp's reads of wp[stage] are complete here, so this arrival (through
-        // the UMMA commit on `consumed`) is also what lets the producer refill it.
-        if (lane == 0) mbar_arrive(&s.unpack_full[stage]);
+        // The warp's reads of wp[stage] completed before this arrival, and the UMMAs
+        // of this group (whose commit frees the load stage) wait for it.
+        if (lane == 0) mbar_arrive(&s.w_full[us]);
+        if (ut == 0 && gi - 8u < 8u) probe_mark(32 + gi - 8u);
         if (++stage == LS) {
           stage = 0;
           phase ^= 1u;
         }
+        if (++us == kUnpacked) us = 0;
       }
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------------ epilogue
+    if constexpr (C::kSplitRegs) regs_claim<C::kRegsHigh>();
     const uint32_t ew = warp - 8;            // 0 .. 4*EWG-1
     const uint32_t q = ew & 3u;              // TMEM lane quarter
     const uint32_t h = ew >> 2;              // column block of this warpgroup
     const uint32_t et = threadIdx.x - 256;   // 0 .. 128*EWG-1
     const uint32_t nl = q * 32 + lane;       // weight row (output column) within the tile
     const uint32_t col0 = h * C::kCols;      // first token column of this thread
-    const uint32_t n_epi = 128 * EWG;
     constexpr uint32_t kPairs = C::kCols / 2;
+    // Vector scale loads need 16-byte-aligned 8-group chunks in every row.
+    const bool vec_sb = (p.G % 8u == 0u) && (p.ldsb % 8u == 0u) &&
+                        ((reinterpret_cast<uintptr_t>(p.sb) & 15u) == 0u);
     uint32_t gi = 0, cursor = 0;
     Work w;
     bool ok = true;
@@ -352,65 +387,76 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
       for (uint32_t j = 0; j < kPairs; ++j) acc[j] = 0ull;
       float bias_sum = 0.f;
 
-      // Weight scale of the first group, then one group ahead.
+      // Weight scales. A scale fetched only one group ahead would expose a full L2
+      // latency every group, so with 16-byte-aligned rows (the usual case) the
+      // scales come in 8-group vectors two windows ahead: `win0` holds the scales
+      // of the next groups (consumed 16 bits at a time), `win1` the 8 after those.
+      const uint16_t* sb_row = p.sb + size_t(n) * p.ldsb;
+      uint4 win0 = make_uint4(0, 0, 0, 0), win1 = make_uint4(0, 0, 0, 0);
       float s_next = 0.f;
       if (n_valid && w.g_begin < w.g_end) {
-        s_next = bf16_bits_to_float(__ldg(p.sb + size_t(n) * p.ldsb + w.g_begin));
+        if (vec_sb) {
+          win0 = __ldg(reinterpret_cast<const uint4*>(sb_row + w.g_begin));
+          if (w.g_begin + 8u < w.g_end) win1 = __ldg(reinterpret_cast<const uint4*>(sb_row + w.g_begin + 8u));
+        } else {
+          s_next = bf16_bits_to_float(__ldg(sb_row + w.g_begin));
+        }
       }
       for (uint32_t g = w.g_begin; g < w.g_end; ++g, ++gi) {
-        const float s_g = s_next * 0.0625f;  // 1/16 undoes the high-nibble placement
-        if (n_valid && g + 1 < w.g_end) {
-          s_next = bf16_bits_to_float(__ldg(p.sb + size_t(n) * p.ldsb + g + 1));
+        float s_g;
+        if (vec_sb) {
+          s_g = __uint_as_float(win0.x << 16) * 0.0625f;  // 1/16: high-nibble placement
+          win0.x = __funnelshift_r(win0.x, win0.y, 16);
+          win0.y = __funnelshift_r(win0.y, win0.z, 16);
+          win0.z = __funnelshift_r(win0.z, win0.w, 16);
+          win0.w >>= 16;
+          if (((g - w.g_begin) & 7u) == 7u) {
+            win0 = win1;
+            if (n_valid && g + 9u < w.g_end) win1 = __ldg(reinterpret_cast<const uint4*>(sb_row + g + 9u));
+          }
+        } else {
+          s_g = s_next * 0.0625f;
+          if (n_valid && g + 1 < w.g_end) s_next = bf16_bits_to_float(__ldg(sb_row + g + 1));
         }
         const uint64_t s2 = f32x2_pack(s_g, s_g);
-        const uint32_t acc_b = gi & 1u;
-        const uint32_t acc_phase = (gi >> 1) & 1u;
-        if (et == 0) {
-          s.epi_ok =
-              mbar_wait(&s.tmem_full[acc_b], acc_phase, abort, kStatusTimeoutEpilogue) ? 1u : 0u;
-        }
-        named_barrier_sync(1, n_epi);
-        if (*reinterpret_cast<volatile uint32_t*>(&s.epi_ok) == 0u) {
+        const uint32_t acc_b = gi % kAcc;
+        if (!mbar_wait_warp(&s.mma_done[gi % kDoneRing], done_parity(gi), abort,
+                            kStatusTimeoutEpilogue)) {
           ok = false;
           break;
         }
+        if (et == 0 && gi - 8u < 8u) probe_mark(8 + gi - 8u);
         tc_fence_after_sync();
         const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc_b * BT + col0;
+        // All of this thread's columns in one wait, then the bias re-arm is issued
+        // and overlaps the arithmetic; the accumulator is handed back after both.
+        uint32_t r[C::kCols];
 #pragma unroll
         for (uint32_t c0 = 0; c0 < C::kCols; c0 += C::kChunk) {
-          uint32_t r[C::kChunk];
-          if constexpr (C::kChunk == 16) {
-            tmem_ld_32x32b_x16(t_row + c0, r);
-          } else {
-            tmem_ld_32x32b_x32(t_row + c0, r);
-          }
-          tmem_ld_wait();
-          if (c0 + C::kChunk == C::kCols) {
-            // Every column of this thread has been read: re-arm the bias, then hand
-            // the accumulator back to the UMMA issuer.
+          tmem_ld_32x32b_x32(t_row + c0, *reinterpret_cast<uint32_t(*)[32]>(r + c0));
+        }
+        tmem_ld_wait();
 #pragma unroll
-            for (uint32_t c = 0; c < C::kCols; c += 8) tmem_st_32x32b_x8_fill(t_row + c, kBiasBits);
-            tmem_st_wait();
-            tc_fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s.tmem_empty[acc_b]);
-          }
+        for (uint32_t c = 0; c < C::kCols; c += 8) tmem_st_32x32b_x8_fill(t_row + c, kBiasBits);
 #pragma unroll
-          for (uint32_t j = 0; j < C::kChunk; j += 2) {
-            acc[(c0 + j) / 2] = f32x2_fma(f32x2_pack(__uint_as_float(r[j]), __uint_as_float(r[j + 1])),
-                                          s2, acc[(c0 + j) / 2]);
-          }
-          if (p.partials != nullptr && n_valid) {
+        for (uint32_t j = 0; j < C::kCols; j += 2) {
+          acc[j / 2] = f32x2_fma(f32x2_pack(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), s2,
+                                 acc[j / 2]);
+        }
+        if (p.partials != nullptr && n_valid) {
 #pragma unroll
-            for (uint32_t j = 0; j < C::kChunk; ++j) {
-              const uint32_t m = w.m0 + col0 + c0 + j;
-              if (m < p.M) {
-                p.partials[(size_t(m) * p.N + n) * p.G + g] =
-                    static_cast<int32_t>(r[j] - kBiasBits) >> 4;
-              }
+          for (uint32_t j = 0; j < C::kCols; ++j) {
+            const uint32_t m = w.m0 + col0 + j;
+            if (m < p.M) {
+              p.partials[(size_t(m) * p.N + n) * p.G + g] = static_cast<int32_t>(r[j] - kBiasBits) >> 4;
             }
           }
         }
+        tmem_st_wait();
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.tmem_empty[acc_b]);
+        if (et == 0 && gi - 8u < 8u) probe_mark(16 + gi - 8u);
         bias_sum += s_g * kBiasF;  // exact: 8 significant bits times 2
         if ((g - w.g_begin) % kBiasFlush == kBiasFlush - 1u || g + 1 == w.g_end) {
           const uint64_t nb = f32x2_pack(-bias_sum, -bias_sum);
@@ -418,37 +464,37 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
           for (uint32_t j = 0; j < kPairs; ++j) acc[j] = f32x2_add(acc[j], nb);
           bias_sum = 0.f;
         }
+        if (et == 0 && gi - 8u < 8u) probe_mark(48 + gi - 8u);
       }
       if (!ok) break;
 
-      {
-        // ---- scale by sa, stage [BT][128] bf16, one TMA store per tile.
-        if (et < BT) s.sa[et] = (w.m0 + et < p.M) ? __ldg(p.sa + w.m0 + et) : 0.f;
-        if (et == 0) tma_store_wait_read<0>();  // previous tile's store has read s.out
-        named_barrier_sync(1, n_epi);
-        uint16_t* o = reinterpret_cast<uint16_t*>(s.out);
+      // ---- scale by sa and store: for each token m the 32 lanes of a warp write 32
+      // consecutive columns (64 contiguous bytes).
+      if (n_valid) {
+        uint16_t* o = p.out + n;
 #pragma unroll
         for (uint32_t j = 0; j < kPairs; ++j) {
           float a0, a1;
           f32x2_unpack(acc[j], a0, a1);
-          o[(col0 + 2 * j) * kRows + nl] =
-              __bfloat16_as_ushort(__float2bfloat16_rn(a0 * s.sa[col0 + 2 * j]));
-          o[(col0 + 2 * j + 1) * kRows + nl] =
-              __bfloat16_as_ushort(__float2bfloat16_rn(a1 * s.sa[col0 + 2 * j + 1]));
-        }
-        fence_proxy_async_smem();
-        named_barrier_sync(1, n_epi);
-        if (et == 0) {
-          tma_store_2d(&p.tm_out, s.out, int32_t(w.n0), int32_t(w.m0));
-          tma_store_commit();
+          const uint32_t m = w.m0 + col0 + 2 * j;
+          if (m < p.M) {
+            o[size_t(m) * p.ldc] = __bfloat16_as_ushort(__float2bfloat16_rn(a0 * __ldg(p.sa + m)));
+          }
+          if (m + 1 < p.M) {
+            o[size_t(m + 1) * p.ldc] =
+                __bfloat16_as_ushort(__float2bfloat16_rn(a1 * __ldg(p.sa + m + 1)));
+          }
         }
       }
     }
-    if (et == 0) tma_store_wait_all<0>();
+  } else {
+    // Warps 2-3 (TMEM allocator, idle) share the producer's warpgroup.
+    if constexpr (C::kSplitRegs) regs_release<C::kRegsLow>();
   }
 
   tc_fence_before_sync();
   __syncthreads();
+  if (threadIdx.x == 0) probe_mark(59);
   if (warp == 2) {
     tc_fence_after_sync();
     tmem_dealloc(tmem_base, C::kTmemCols);

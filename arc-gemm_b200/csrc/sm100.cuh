@@ -54,18 +54,13 @@ constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
 constexpr uint32_t kProbeSlots = 64;  // stamps per CTA
 __device__ unsigned long long* g_arc_probe;
 
-// The buffer pointer is read once per thread (the first stamp); later stamps are a
-// clock read and a store, so they barely perturb the pipeline they measure.
+// A stamp is a clock read, one load of the buffer pointer (an L1 hit after the
+// first) and a store, so it barely perturbs the pipeline it measures.
 __device__ __forceinline__ void probe_mark(uint32_t slot) {
 #if defined(ARC_PROBE)
-  __shared__ unsigned long long* cached;  // one copy per CTA, set by the first stamp
   unsigned long long t;
   asm volatile("mov.u64 %0, %%clock64;" : "=l"(t));
-  unsigned long long* buf = *reinterpret_cast<unsigned long long* volatile*>(&cached);
-  if (buf == nullptr) {
-    buf = g_arc_probe;
-    cached = buf;
-  }
+  unsigned long long* buf = g_arc_probe;
   if (buf != nullptr && slot < kProbeSlots) buf[blockIdx.x * kProbeSlots + slot] = t;
 #else
   (void)slot;
@@ -174,6 +169,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
       }
     }
   }
+}
+
+// Warp-wide bounded wait: lane 0 waits and the outcome is broadcast, so the warp
+// leaves together. Every lane of the warp must call it (it ends in a full-warp
+// shuffle), never from inside a branch that splits the warp.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity,
+                                               volatile uint32_t* abort, uint32_t err_bit) {
+  uint32_t ok = 0;
+  if ((threadIdx.x & 31u) == 0u) ok = mbar_wait(bar, parity, abort, err_bit) ? 1u : 0u;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0u;
+}
+
+// Per-warpgroup register budget moves (all four warps of a warpgroup execute the
+// same one). An increase waits until other warpgroups have released enough of the
+// registers the CTA was launched with, so the shares must add up to at most
+// threads x launch registers.
+template <uint32_t N>
+__device__ __forceinline__ void regs_release() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_claim() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // Bounded wait that ignores the abort flag: used on the teardown path to let

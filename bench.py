@@ -306,7 +306,20 @@ def run_ours(args, wl, world, rank, local):
     flush = None
     if n_sets == 1:  # inputs alone exceed 2x L2 only for the large configs
         flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.int32, device=device)
-    use_graph = flush is None and not args.no_graph
+    gather = args.allgather and world > 1
+    if gather:
+        # Each step also all-gathers the bf16 output over NCCL into [world*M, N/world]
+        # (arc.parallel.gather_columns' layout); eager launches, no graph.
+        import torch.distributed as dist
+
+        gathered = torch.empty((world * M, N), dtype=torch.bfloat16, device=device)
+        local_call = call
+
+        def call(s):
+            out = local_call(s)
+            dist.all_gather_into_tensor(gathered, out)
+            return gathered
+    use_graph = flush is None and not args.no_graph and not gather
     stream = torch.cuda.Stream(device)
     peaks = load_peaks()
 
@@ -404,7 +417,8 @@ def run_ours(args, wl, world, rank, local):
                            (n_sets, n_sets * in_bytes / 1e6)) if flush is None
                        else "L2 flushed (512 MB write) before every timed step",
                        launch="K launches in one CUDA graph" if use_graph else "eager launches",
-                       allgather=bool(args.allgather)),
+                       allgather=("NCCL all_gather_into_tensor of the bf16 output every step"
+                                  if gather else False)),
         "hbm_gbs": world * step_bytes / (step_ms * 1e-3) / 1e9,
         "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                      "frac": achieved / peak, "traffic": traffic,
