@@ -132,8 +132,8 @@ constexpr size_t decode_smem_bytes() {
 
 // The persistent-tile instantiations the dispatcher can pick (M > 32).
 #define ARC_A8W4_VARIANTS(X) \
-  X(64, 1, 8)                \
-  X(128, 2, 7)
+  X(64, 1, 4)                \
+  X(128, 2, 3)
 
 int init_device(int dev) {
   DeviceState& st = g_dev[dev];
@@ -319,8 +319,8 @@ int plan_a8w4(int M, int N, int K, int sms, int max_c2, int max_c4, arc_a8w4_pla
   plan->weight_rows = static_cast<int>(arcb::a8w4::kRows);
   plan->k_split = 1;
   plan->grid = static_cast<int>(tiles < static_cast<uint32_t>(sms) ? tiles : sms);
-  plan->load_stages = bt == 64 ? 8 : 7;
-  plan->groups_per_stage = 1;
+  plan->load_stages = bt == 64 ? 4 : 3;
+  plan->groups_per_stage = static_cast<int>(arcb::a8w4::kGps);
   return ARC_OK;
 }
 
@@ -554,7 +554,7 @@ int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uin
     return st;
   }
   if (int st = encode_2d(&p.tm_wp, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Wp, K / 2, N, K / 2,
-                         Q::kPackedRow, R, CU_TENSOR_MAP_SWIZZLE_NONE, "Wp")) {
+                         Q::kPackedRow * Q::kGps, R, CU_TENSOR_MAP_SWIZZLE_NONE, "Wp")) {
     return st;
   }
   p.sa = sa;
@@ -573,11 +573,11 @@ int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uin
   p.num_tiles = p.tiles_m * p.tiles_n;
   const uint32_t grid = static_cast<uint32_t>(plan.grid);
   if (BT == 64) {
-    e = launch_ex(Q::gemm_a8w4_kernel<64, 1, 8>, p, grid, Q::Cfg<64, 1, 8>::kThreads,
-                  a8w4_smem_bytes<64, 1, 8>(), 1, stream);
+    e = launch_ex(Q::gemm_a8w4_kernel<64, 1, 4>, p, grid, Q::Cfg<64, 1, 4>::kThreads,
+                  a8w4_smem_bytes<64, 1, 4>(), 1, stream);
   } else {
-    e = launch_ex(Q::gemm_a8w4_kernel<128, 2, 7>, p, grid, Q::Cfg<128, 2, 7>::kThreads,
-                  a8w4_smem_bytes<128, 2, 7>(), 1, stream);
+    e = launch_ex(Q::gemm_a8w4_kernel<128, 2, 3>, p, grid, Q::Cfg<128, 2, 3>::kThreads,
+                  a8w4_smem_bytes<128, 2, 3>(), 1, stream);
   }
   if (e != cudaSuccess) return cuda_fail(e, "gemm_a8w4_kernel launch");
   return ARC_OK;

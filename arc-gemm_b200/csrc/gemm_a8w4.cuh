@@ -25,24 +25,28 @@
 // accumulator holds 16*P (|16P| <= 16*128*127*8 < 2^22, exact in int32 and fp32) and
 // the factor 1/16 is folded into the (exact) scale multiply.
 //
+// Work moves through the pipeline in STEPS of two K-groups (kGps): one load stage,
+// one unpacked stage, one commit and one accumulator pair per step, so every
+// mbarrier hand-off (~250 cycles between warps on B200) is paid once per 256 K.
+//
 // Roles (256 + 128*EWG threads):
-//   warp 0        TMA producer: token tile [BT x 128 B] (SW128) + packed weight tile
-//                 [128 x 64 B] per K-group into an LS-stage load ring
-//   warp 1        UMMA issuer: 4 x tcgen05.mma kind::i8 M=128 N=BT K=32 per group into
-//                 one of kAcc TMEM accumulators (a fresh int32 partial per group, on
-//                 top of the bias described at kBiasBits), then ONE commit per group
+//   warp 0        TMA producer: per step two token boxes [BT x 128 B] (SW128) and one
+//                 packed weight box [128 x 128 B] (both groups) into an LS-stage ring
+//   warp 1        UMMA issuer: per group 4 x tcgen05.mma kind::i8 M=128 N=BT K=32 into
+//                 its own TMEM accumulator (a fresh int32 partial per group, on top of
+//                 the bias described at kBiasBits), then ONE commit per step
 //   warp 2        TMEM allocator
 //   warp 3        idle
 //   warps 4-7     unpack warpgroup: packed smem -> int8 SW128 smem (kUnpacked-stage ring)
-//   warps 8-...   epilogue warpgroup(s): tcgen05.ld partial, re-arm the bias, fp32
+//   warps 8-...   epilogue warpgroup(s): tcgen05.ld partials, re-arm the bias, fp32
 //                 scale-accumulate on packed f32x2 pairs, bf16 stores to global
 //
-// Synchronisation: the single per-group commit lands on mma_done[gi % 8] (gi counts
-// the CTA's groups). It tells the producer that load stage gi % LS is free again
-// (waited LS groups later), the unpack warps that unpacked stage gi % kUnpacked is
-// free (kUnpacked groups later) and the epilogue that accumulator gi % kAcc holds
-// group gi. Each waiter is at most one phase behind the barrier it tests, which the
-// bounds LS, kUnpacked <= 8 and kAcc < 8 guarantee.
+// Synchronisation: the per-step commit lands on mma_done[si % 8] (si counts the CTA's
+// steps). It tells the producer that load stage si % LS is free again (waited LS
+// steps later), the unpack warps that unpacked stage si % kUnpacked is free
+// (kUnpacked steps later) and the epilogue that accumulator pair si % 2 holds the
+// step's partials. Each waiter is at most one phase behind the barrier it tests,
+// which the bounds LS, kUnpacked <= 8 and 2 accumulator pairs < 8 guarantee.
 //
 // Work decomposition: persistent CTAs stride over (token tile, weight tile) pairs;
 // each tile covers all K-groups. Decode-sized M (<= 32) uses the dedicated kernel in
@@ -58,9 +62,10 @@ constexpr uint32_t kRows = 128;        // UMMA M: weight rows per tile (TMEM lan
 constexpr uint32_t kGroupK = 128;      // K elements per scale group = one 128-byte row
 constexpr uint32_t kPackedRow = 64;    // bytes of packed int4 per row per group
 constexpr uint32_t kUmmaK = 32;        // K per kind::i8 UMMA (32 bytes)
-constexpr uint32_t kUnpacked = 3;      // unpacked weight stages
-constexpr uint32_t kAcc = 4;           // TMEM accumulators
-constexpr uint32_t kDoneRing = 8;      // per-group completion barriers
+constexpr uint32_t kGps = 2;           // K-groups per pipeline step
+constexpr uint32_t kUnpacked = 2;      // unpacked weight stages (steps)
+constexpr uint32_t kAccPairs = 2;      // TMEM accumulator pairs (steps in flight)
+constexpr uint32_t kDoneRing = 8;      // per-step completion barriers
 
 // Accumulator bias. Between uses every int32 accumulator column in TMEM holds
 // kBiasBits, the bit pattern of kBiasF = 1.5 * 2^23, and the UMMAs of a K-group
@@ -74,10 +79,11 @@ constexpr float kBiasF = 12582912.0f;
 // group, with the running value never more than kBiasFlush biased terms away from the
 // result (rounding error ~2^-9 of a typical partial's scale, far below a bf16 ulp).
 constexpr uint32_t kBiasFlush = 4;
+static_assert(kBiasFlush % kGps == 0, "flush on step boundaries");
 
 struct Params {
   CUtensorMap tm_tok;  // A  [M][K] u8 view of int8, box {128, BT}, SW128
-  CUtensorMap tm_wp;   // Wp [N][K/2] u8, box {64, 128}, no swizzle
+  CUtensorMap tm_wp;   // Wp [N][K/2] u8, box {128, 128} (two groups), no swizzle
   const float* sa;
   const uint16_t* sb;
   uint16_t* out;
@@ -93,11 +99,15 @@ template <uint32_t BT, uint32_t EWG, uint32_t LS>
 struct Cfg {
   static_assert(BT == 64 || BT == 128, "token tile");
   static_assert(EWG == 1 || EWG == 2, "epilogue warpgroups");
-  static_assert(LS >= 2 && LS <= kDoneRing && kUnpacked <= kDoneRing && kAcc < kDoneRing,
+  static_assert(LS >= 2 && LS <= kDoneRing && kUnpacked <= kDoneRing && kAccPairs < kDoneRing,
                 "each waiter must stay within one phase of its completion barrier");
   static constexpr uint32_t kThreads = 256 + 128 * EWG;
   static constexpr uint32_t kCols = BT / EWG;               // columns per epilogue thread
   static constexpr uint32_t kChunk = 32;                    // TMEM columns per load
+  static constexpr uint32_t kTmemCols = kAccPairs * kGps * BT;  // 256 or 512
+  static constexpr uint32_t kTokBytes = BT * kGroupK;       // one group's token box
+  static constexpr uint32_t kWpBytes = kRows * kPackedRow * kGps;
+  static constexpr uint32_t kWBytes = kRows * kGroupK;      // one group's unpacked tile
   // Register budget: the producer/UMMA and unpack warpgroups drop to kRegsLow and
   // the epilogue warpgroup(s) rise to kRegsHigh, out of kLaunchRegs per thread at
   // launch (the most 1 CTA/SM allows; the host checks the compiled count).
@@ -107,29 +117,25 @@ struct Cfg {
   static constexpr uint32_t kRegsHigh = EWG == 2 ? 176 : 232;
   static_assert(256 * kRegsLow + 128 * EWG * kRegsHigh <= kThreads * kLaunchRegs,
                 "register shares exceed the launch budget");
-  static constexpr uint32_t kTmemCols = kAcc * BT;          // 256 or 512
-  static constexpr uint32_t kTokBytes = BT * kGroupK;
-  static constexpr uint32_t kWpBytes = kRows * kPackedRow;
-  static constexpr uint32_t kWBytes = kRows * kGroupK;
   static_assert(kCols % kChunk == 0, "epilogue column split");
 };
 
 template <uint32_t BT, uint32_t EWG, uint32_t LS>
 struct alignas(1024) Smem {
   using C = Cfg<BT, EWG, LS>;
-  uint8_t w[kUnpacked][C::kWBytes];             // unpacked int8, SW128 (UMMA A)
-  uint8_t tok[LS][C::kTokBytes];                // tokens, SW128 (UMMA B)
-  uint8_t wp[LS][C::kWpBytes];                  // packed int4 straight from TMA
+  uint8_t w[kUnpacked][kGps][C::kWBytes];       // unpacked int8, SW128 (UMMA A)
+  uint8_t tok[LS][kGps][C::kTokBytes];          // tokens, SW128 (UMMA B)
+  uint8_t wp[LS][C::kWpBytes];                  // packed int4 [128 rows][2 groups x 64 B]
   uint64_t load_full[LS];                       // TMA bytes landed (tokens + packed W)
   uint64_t w_full[kUnpacked];                   // 4 unpack warps wrote w[u]
-  uint64_t mma_done[kDoneRing];                 // the UMMAs of group gi retired
-  uint64_t tmem_empty[kAcc];                    // epilogue read accumulator a
+  uint64_t mma_done[kDoneRing];                 // the UMMAs of step si retired
+  uint64_t tmem_empty[kAccPairs];               // epilogue read accumulator pair a
   uint32_t tmem_base;
   uint32_t abort;
 };
 
-// Parity of the completion of mma_done that belongs to group gi.
-__device__ __forceinline__ uint32_t done_parity(uint32_t gi) { return (gi / kDoneRing) & 1u; }
+// Parity of the completion of mma_done that belongs to step si.
+__device__ __forceinline__ uint32_t done_parity(uint32_t si) { return (si / kDoneRing) & 1u; }
 
 // ---------------------------------------------------------------------------------
 // Work decomposition
@@ -185,11 +191,12 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
   const uint32_t warp = warp_idx_sync();
   const uint32_t lane = threadIdx.x & 31u;
   volatile uint32_t* abort = &s.abort;
+  const uint32_t steps_per_tile = (p.G + kGps - 1) / kGps;
 
-  // Probe stamps (probe build only): steady-state groups 8..15 of the first tile.
-  //   0-7 UMMA waits passed   8-15 partial seen by the epilogue   16-23 accumulator
-  //   released   24-31 unpack waits passed   32-39 stage unpacked   40-47 loads
-  //   issued   48-55 group accumulated   56 entry   57 prologue done   59 exit
+  // Probe stamps (probe build only): steady-state steps 4..11 of the first tile.
+  //   0-7 UMMA waits passed   8-15 partials seen by the epilogue   16-23 accumulator
+  //   pair released   24-31 unpack waits passed   32-39 stage unpacked   40-47 loads
+  //   issued   48-55 step accumulated   56 entry   57 prologue done   59 exit
   if (threadIdx.x == 0) probe_mark(56);
   pdl_launch_dependents();
   if (warp == 0 && lane == 0) {
@@ -198,7 +205,7 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
     for (uint32_t i = 0; i < LS; ++i) mbar_init(&s.load_full[i], 1);
     for (uint32_t i = 0; i < kUnpacked; ++i) mbar_init(&s.w_full[i], 4);  // one per unpack warp
     for (uint32_t i = 0; i < kDoneRing; ++i) mbar_init(&s.mma_done[i], 1);  // UMMA commit
-    for (uint32_t i = 0; i < kAcc; ++i) mbar_init(&s.tmem_empty[i], 4 * EWG);
+    for (uint32_t i = 0; i < kAccPairs; ++i) mbar_init(&s.tmem_empty[i], 4 * EWG);
     s.abort = 0;
     fence_barrier_init();
   }
@@ -215,7 +222,7 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
     const uint32_t ew = warp - 8;
     const uint32_t row = tmem_base + (((ew & 3u) * 32u) << 16) + (ew >> 2) * C::kCols;
 #pragma unroll
-    for (uint32_t b = 0; b < kAcc; ++b) {
+    for (uint32_t b = 0; b < kAccPairs * kGps; ++b) {
 #pragma unroll
       for (uint32_t c = 0; c < C::kCols; c += 8) tmem_st_32x32b_x8_fill(row + b * BT + c, kBiasBits);
     }
@@ -228,40 +235,47 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
   // dependent launch); global memory is only touched after it has completed.
   pdl_wait();
   if (threadIdx.x == 0) probe_mark(57);
+
   // Register moves sit inside each role's branch, so that the compiler gives every
   // role's code the budget of that role.
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if constexpr (C::kSplitRegs) regs_release<C::kRegsLow>();
     if (lane == 0) {
-      uint32_t stage = 0, phase = 0, gi = 0, cursor = 0;
-      const uint32_t tx = C::kTokBytes + C::kWpBytes;
+      uint32_t stage = 0, si = 0, cursor = 0;
       Work w;
       bool ok = true;
       while (ok && next_work<BT>(p, cursor, w)) {
-        for (uint32_t g = w.g_begin; g < w.g_end; ++g, ++gi) {
-          // Stage `stage` last served group gi - LS; its UMMAs (which ran after the
+        for (uint32_t t = 0; t < steps_per_tile; ++t, ++si) {
+          // Stage `stage` last served step si - LS; its UMMAs (which ran after the
           // unpack warps had read the packed half) must have retired.
-          if (gi >= LS && !mbar_wait(&s.mma_done[(gi - LS) % kDoneRing], done_parity(gi - LS),
+          if (si >= LS && !mbar_wait(&s.mma_done[(si - LS) % kDoneRing], done_parity(si - LS),
                                      abort, kStatusTimeoutProducer)) {
             ok = false;
             break;
           }
-          if (gi - 8u < 8u) probe_mark(40 + gi - 8u);
-          mbar_arrive_expect_tx(&s.load_full[stage], tx);
-          tma_load_2d(&p.tm_tok, &s.load_full[stage], s.tok[stage], int32_t(g * kGroupK),
-                      int32_t(w.m0), kCacheEvictLast);
-          tma_load_2d(&p.tm_wp, &s.load_full[stage], s.wp[stage], int32_t(g * kPackedRow),
-                      int32_t(w.n0), kCacheEvictFirst);
-          if (++stage == LS) {
-            stage = 0;
-            phase ^= 1u;
+          if (si - 4u < 8u) probe_mark(40 + si - 4u);
+          const uint32_t g0 = w.g_begin + t * kGps;
+          // The last step of an odd group count has one real group: its second token
+          // box is not loaded (the packed box is partly in bounds and is credited in
+          // full, zero fill included).
+          const uint32_t real = min(kGps, w.g_end - g0);
+          mbar_arrive_expect_tx(&s.load_full[stage], real * C::kTokBytes + C::kWpBytes);
+#pragma unroll
+          for (uint32_t h = 0; h < kGps; ++h) {
+            if (h < real) {
+              tma_load_2d(&p.tm_tok, &s.load_full[stage], s.tok[stage][h],
+                          int32_t((g0 + h) * kGroupK), int32_t(w.m0), kCacheEvictLast);
+            }
           }
+          tma_load_2d(&p.tm_wp, &s.load_full[stage], s.wp[stage], int32_t(g0 * kPackedRow),
+                      int32_t(w.n0), kCacheEvictFirst);
+          if (++stage == LS) stage = 0;
         }
       }
       // Let the loads still in flight land before the CTA may exit.
-      const uint32_t n_drain = gi < LS ? gi : LS;
-      for (uint32_t i = gi - n_drain; i < gi; ++i) {
+      const uint32_t n_drain = si < LS ? si : LS;
+      for (uint32_t i = si - n_drain; i < si; ++i) {
         mbar_drain(&s.load_full[i % LS], (i / LS) & 1u);
       }
     }
@@ -270,31 +284,42 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
     if constexpr (C::kSplitRegs) regs_release<C::kRegsLow>();
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_s8_s32(kRows, BT);
-      uint32_t stage = 0, phase = 0, us = 0, uphase = 0, gi = 0, cursor = 0;
+      uint32_t stage = 0, phase = 0, us = 0, uphase = 0, si = 0, cursor = 0;
       Work w;
       bool ok = true;
       while (ok && next_work<BT>(p, cursor, w)) {
-        for (uint32_t g = w.g_begin; g < w.g_end; ++g, ++gi) {
-          const uint32_t acc = gi % kAcc;
-          if ((gi >= kAcc && !mbar_wait(&s.tmem_empty[acc], (gi / kAcc - 1u) & 1u, abort,
-                                        kStatusTimeoutMma)) ||
-              !mbar_wait(&s.w_full[us], uphase, abort, kStatusTimeoutMma) ||
-              !mbar_wait(&s.load_full[stage], phase, abort, kStatusTimeoutMma)) {
+        for (uint32_t t = 0; t < steps_per_tile; ++t, ++si) {
+          const uint32_t pair = si % kAccPairs;
+          const uint32_t acc_parity = (si / kAccPairs - 1u) & 1u;
+          // Test all three first (their latencies overlap), block only on the others.
+          const uint32_t t_acc = si >= kAccPairs ? mbar_test(&s.tmem_empty[pair], acc_parity) : 1u;
+          const uint32_t t_w = mbar_test(&s.w_full[us], uphase);
+          const uint32_t t_ld = mbar_test(&s.load_full[stage], phase);
+          if ((t_acc == 0u && !mbar_wait(&s.tmem_empty[pair], acc_parity, abort, kStatusTimeoutMma)) ||
+              (t_w == 0u && !mbar_wait(&s.w_full[us], uphase, abort, kStatusTimeoutMma)) ||
+              (t_ld == 0u && !mbar_wait(&s.load_full[stage], phase, abort, kStatusTimeoutMma))) {
             ok = false;
             break;
           }
-          if (gi - 8u < 8u) probe_mark(gi - 8u);
+          if (si - 4u < 8u) probe_mark(si - 4u);
           tc_fence_after_sync();
-          const uint64_t adesc = make_sw128_kmajor_desc(s.w[us]);
-          const uint64_t bdesc = make_sw128_kmajor_desc(s.tok[stage]);
-          const uint32_t d_tmem = tmem_base + acc * BT;
-          // Every UMMA accumulates: the group starts from the bias the epilogue left.
+          // A group past K (odd group count) is skipped: its accumulator keeps the bias
+          // for the next tile, and the epilogue skips it too.
+          const uint32_t real = min(kGps, w.g_end - (w.g_begin + t * kGps));
 #pragma unroll
-          for (uint32_t k = 0; k < kGroupK / kUmmaK; ++k) {
-            umma_s8(d_tmem, desc_advance(adesc, k * kUmmaK), desc_advance(bdesc, k * kUmmaK), idesc,
-                    1u);
+          for (uint32_t h = 0; h < kGps; ++h) {
+            if (h >= real) break;
+            const uint64_t adesc = make_sw128_kmajor_desc(s.w[us][h]);
+            const uint64_t bdesc = make_sw128_kmajor_desc(s.tok[stage][h]);
+            const uint32_t d_tmem = tmem_base + (pair * kGps + h) * BT;
+            // Every UMMA accumulates: the group starts from the bias the epilogue left.
+#pragma unroll
+            for (uint32_t k = 0; k < kGroupK / kUmmaK; ++k) {
+              umma_s8(d_tmem, desc_advance(adesc, k * kUmmaK), desc_advance(bdesc, k * kUmmaK),
+                      idesc, 1u);
+            }
           }
-          umma_commit(&s.mma_done[gi % kDoneRing]);
+          umma_commit(&s.mma_done[si % kDoneRing]);
           if (++stage == LS) {
             stage = 0;
             phase ^= 1u;
@@ -306,56 +331,70 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
         }
       }
       // The last commit covers every UMMA this thread issued.
-      if (gi > 0u) mbar_drain(&s.mma_done[(gi - 1u) % kDoneRing], done_parity(gi - 1u));
+      if (si > 0u) mbar_drain(&s.mma_done[(si - 1u) % kDoneRing], done_parity(si - 1u));
     }
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------ unpack warpgroup
     if constexpr (C::kSplitRegs) regs_release<C::kRegsLow>();
     const uint32_t ut = threadIdx.x - 128;  // 0..127
-    uint32_t stage = 0, phase = 0, us = 0, gi = 0, cursor = 0;
-    // Each warp waits for itself (no warpgroup barrier per group).
-    // Thread ut converts 16-byte chunks id = i*128 + ut (i < 4) of the 8 KB packed
-    // tile: row r = id / 4, packed bytes [16c, 16c+16) with c = id % 4, which become
+    uint32_t stage = 0, phase = 0, us = 0, si = 0, cursor = 0;
+    // Each warp waits for itself (no warpgroup barrier per step). Per group h of a
+    // step, thread ut converts 16-byte chunks id = i*128 + ut (i < 4) of the packed
+    // tile: row r = id / 4, packed bytes [64h + 16c, +16) with c = id % 4, which become
     // the 32 int8 bytes [32c, 32c+32) of row r = swizzled 16-byte chunks 2c and 2c+1.
-    // Reads: a warp covers 512 contiguous bytes. Writes: a quarter-warp covers two
-    // rows whose chunk sets {2c ^ (r&7)} are the even and the odd chunks: no conflicts.
+    // Reads: a warp covers 8 rows x 64 contiguous bytes. Writes: a quarter-warp
+    // covers two rows whose chunk sets {2c ^ (r&7)} are the even and the odd chunks.
     const uint32_t c16 = ut & 3u;
     Work w;
     bool ok = true;
     while (ok && next_work<BT>(p, cursor, w)) {
-      for (uint32_t g = w.g_begin; g < w.g_end; ++g, ++gi) {
-        // Packed tile landed, and the UMMAs that read w[us] last time have retired.
-        if (!mbar_wait_warp(&s.load_full[stage], phase, abort, kStatusTimeoutUnpack) ||
-            (gi >= kUnpacked &&
-             !mbar_wait_warp(&s.mma_done[(gi - kUnpacked) % kDoneRing], done_parity(gi - kUnpacked),
-                             abort, kStatusTimeoutUnpack))) {
+      for (uint32_t t = 0; t < steps_per_tile; ++t, ++si) {
+        // Packed tile landed, and the UMMAs that read w[us] last time have retired
+        // (both tested at once by lane 0).
+        uint32_t t1 = 1u, t2 = 1u;
+        if (lane == 0) {
+          t1 = mbar_test(&s.load_full[stage], phase);
+          if (si >= kUnpacked) t2 = mbar_test(&s.mma_done[(si - kUnpacked) % kDoneRing], done_parity(si - kUnpacked));
+        }
+        if (!mbar_wait_warp2(&s.load_full[stage], phase, t1,
+                             &s.mma_done[(si - kUnpacked) % kDoneRing], done_parity(si - kUnpacked), t2,
+                             abort, kStatusTimeoutUnpack)) {
           ok = false;
           break;
         }
-        if (ut == 0 && gi - 8u < 8u) probe_mark(24 + gi - 8u);
+        if (ut == 0 && si - 4u < 8u) probe_mark(24 + si - 4u);
         const uint8_t* src = s.wp[stage];
-        uint8_t* dst = s.w[us];
-        uint4 x[4];
+        uint4 x[kGps][4];
 #pragma unroll
-        for (uint32_t i = 0; i < 4; ++i) {
-          x[i] = *reinterpret_cast<const uint4*>(src + (i * 128u + ut) * 16u);
+        for (uint32_t h = 0; h < kGps; ++h) {
+#pragma unroll
+          for (uint32_t i = 0; i < 4; ++i) {
+            const uint32_t id = i * 128u + ut;
+            x[h][i] = *reinterpret_cast<const uint4*>(src + (id >> 2) * (kGps * kPackedRow) +
+                                                      h * kPackedRow + c16 * 16u);
+          }
         }
 #pragma unroll
-        for (uint32_t i = 0; i < 4; ++i) {
-          const uint32_t r = (i * 128u + ut) >> 2;
-          const uint2 a = expand_int4x8(x[i].x), b = expand_int4x8(x[i].y);
-          const uint2 c = expand_int4x8(x[i].z), d = expand_int4x8(x[i].w);
-          uint8_t* row = dst + r * kGroupK;
-          *reinterpret_cast<uint4*>(row + (((2u * c16) ^ (r & 7u)) << 4)) = make_uint4(a.x, a.y, b.x, b.y);
-          *reinterpret_cast<uint4*>(row + (((2u * c16 + 1u) ^ (r & 7u)) << 4)) =
-              make_uint4(c.x, c.y, d.x, d.y);
+        for (uint32_t h = 0; h < kGps; ++h) {
+          uint8_t* dst = s.w[us][h];
+#pragma unroll
+          for (uint32_t i = 0; i < 4; ++i) {
+            const uint32_t r = (i * 128u + ut) >> 2;
+            const uint2 a = expand_int4x8(x[h][i].x), b = expand_int4x8(x[h][i].y);
+            const uint2 c = expand_int4x8(x[h][i].z), d = expand_int4x8(x[h][i].w);
+            uint8_t* row = dst + r * kGroupK;
+            *reinterpret_cast<uint4*>(row + (((2u * c16) ^ (r & 7u)) << 4)) =
+                make_uint4(a.x, a.y, b.x, b.y);
+            *reinterpret_cast<uint4*>(row + (((2u * c16 + 1u) ^ (r & 7u)) << 4)) =
+                make_uint4(c.x, c.y, d.x, d.y);
+          }
         }
         fence_proxy_async_smem();
         __syncwarp();
         // The warp's reads of wp[stage] completed before this arrival, and the UMMAs
-        // of this group (whose commit frees the load stage) wait for it.
+        // of this step (whose commit frees the load stage) wait for it.
         if (lane == 0) mbar_arrive(&s.w_full[us]);
-        if (ut == 0 && gi - 8u < 8u) probe_mark(32 + gi - 8u);
+        if (ut == 0 && si - 4u < 8u) probe_mark(32 + si - 4u);
         if (++stage == LS) {
           stage = 0;
           phase ^= 1u;
@@ -368,15 +407,16 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
     if constexpr (C::kSplitRegs) regs_claim<C::kRegsHigh>();
     const uint32_t ew = warp - 8;            // 0 .. 4*EWG-1
     const uint32_t q = ew & 3u;              // TMEM lane quarter
-    const uint32_t h = ew >> 2;              // column block of this warpgroup
+    const uint32_t hh = ew >> 2;             // column block of this warpgroup
     const uint32_t et = threadIdx.x - 256;   // 0 .. 128*EWG-1
     const uint32_t nl = q * 32 + lane;       // weight row (output column) within the tile
-    const uint32_t col0 = h * C::kCols;      // first token column of this thread
+    const uint32_t col0 = hh * C::kCols;     // first token column of this thread
     constexpr uint32_t kPairs = C::kCols / 2;
     // Vector scale loads need 16-byte-aligned 8-group chunks in every row.
     const bool vec_sb = (p.G % 8u == 0u) && (p.ldsb % 8u == 0u) &&
                         ((reinterpret_cast<uintptr_t>(p.sb) & 15u) == 0u);
-    uint32_t gi = 0, cursor = 0;
+    uint32_t si = 0, cursor = 0;
+    uint32_t pre = 0;  // lane 0: step si's partials seen complete by an early test
     Work w;
     bool ok = true;
     while (ok && next_work<BT>(p, cursor, w)) {
@@ -402,69 +442,82 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
           s_next = bf16_bits_to_float(__ldg(sb_row + w.g_begin));
         }
       }
-      for (uint32_t g = w.g_begin; g < w.g_end; ++g, ++gi) {
-        float s_g;
-        if (vec_sb) {
-          s_g = __uint_as_float(win0.x << 16) * 0.0625f;  // 1/16: high-nibble placement
-          win0.x = __funnelshift_r(win0.x, win0.y, 16);
-          win0.y = __funnelshift_r(win0.y, win0.z, 16);
-          win0.z = __funnelshift_r(win0.z, win0.w, 16);
-          win0.w >>= 16;
-          if (((g - w.g_begin) & 7u) == 7u) {
-            win0 = win1;
-            if (n_valid && g + 9u < w.g_end) win1 = __ldg(reinterpret_cast<const uint4*>(sb_row + g + 9u));
-          }
-        } else {
-          s_g = s_next * 0.0625f;
-          if (n_valid && g + 1 < w.g_end) s_next = bf16_bits_to_float(__ldg(sb_row + g + 1));
-        }
-        const uint64_t s2 = f32x2_pack(s_g, s_g);
-        const uint32_t acc_b = gi % kAcc;
-        if (!mbar_wait_warp(&s.mma_done[gi % kDoneRing], done_parity(gi), abort,
-                            kStatusTimeoutEpilogue)) {
+      for (uint32_t t = 0; t < steps_per_tile; ++t, ++si) {
+        const uint32_t pair = si % kAccPairs;
+        if (!mbar_wait_warp2(&s.mma_done[si % kDoneRing], done_parity(si), pre,
+                             &s.mma_done[si % kDoneRing], done_parity(si), 1u, abort,
+                             kStatusTimeoutEpilogue)) {
           ok = false;
           break;
         }
-        if (et == 0 && gi - 8u < 8u) probe_mark(8 + gi - 8u);
+        if (et == 0 && si - 4u < 8u) probe_mark(8 + si - 4u);
         tc_fence_after_sync();
-        const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc_b * BT + col0;
-        // All of this thread's columns in one wait, then the bias re-arm is issued
-        // and overlaps the arithmetic; the accumulator is handed back after both.
-        uint32_t r[C::kCols];
 #pragma unroll
-        for (uint32_t c0 = 0; c0 < C::kCols; c0 += C::kChunk) {
-          tmem_ld_32x32b_x32(t_row + c0, *reinterpret_cast<uint32_t(*)[32]>(r + c0));
-        }
-        tmem_ld_wait();
+        for (uint32_t h = 0; h < kGps; ++h) {
+          const uint32_t g = w.g_begin + t * kGps + h;
+          if (g >= w.g_end) break;  // past K: uniform across the CTA
+          float s_g;
+          if (vec_sb) {
+            s_g = __uint_as_float(win0.x << 16) * 0.0625f;  // 1/16: high-nibble placement
+            win0.x = __funnelshift_r(win0.x, win0.y, 16);
+            win0.y = __funnelshift_r(win0.y, win0.z, 16);
+            win0.z = __funnelshift_r(win0.z, win0.w, 16);
+            win0.w >>= 16;
+            if (((g - w.g_begin) & 7u) == 7u) {
+              win0 = win1;
+              if (n_valid && g + 9u < w.g_end) {
+                win1 = __ldg(reinterpret_cast<const uint4*>(sb_row + g + 9u));
+              }
+            }
+          } else {
+            s_g = s_next * 0.0625f;
+            if (n_valid && g + 1 < w.g_end) s_next = bf16_bits_to_float(__ldg(sb_row + g + 1));
+          }
+          const uint64_t s2 = f32x2_pack(s_g, s_g);
+          const uint32_t t_row = tmem_base + ((q * 32u) << 16) + (pair * kGps + h) * BT + col0;
+          // All of this thread's columns of the group in one wait; the bias re-arm is
+          // issued right away and overlaps the arithmetic.
+          uint32_t r[C::kCols];
 #pragma unroll
-        for (uint32_t c = 0; c < C::kCols; c += 8) tmem_st_32x32b_x8_fill(t_row + c, kBiasBits);
+          for (uint32_t c0 = 0; c0 < C::kCols; c0 += C::kChunk) {
+            tmem_ld_32x32b_x32(t_row + c0, *reinterpret_cast<uint32_t(*)[32]>(r + c0));
+          }
+          // Ask early whether the next step's partials are ready; the answer arrives
+          // while the loads are in flight.
+          if (h == 0 && lane == 0) pre = mbar_test(&s.mma_done[(si + 1u) % kDoneRing], done_parity(si + 1u));
+          tmem_ld_wait();
 #pragma unroll
-        for (uint32_t j = 0; j < C::kCols; j += 2) {
-          acc[j / 2] = f32x2_fma(f32x2_pack(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), s2,
-                                 acc[j / 2]);
-        }
-        if (p.partials != nullptr && n_valid) {
+          for (uint32_t c = 0; c < C::kCols; c += 8) tmem_st_32x32b_x8_fill(t_row + c, kBiasBits);
 #pragma unroll
-          for (uint32_t j = 0; j < C::kCols; ++j) {
-            const uint32_t m = w.m0 + col0 + j;
-            if (m < p.M) {
-              p.partials[(size_t(m) * p.N + n) * p.G + g] = static_cast<int32_t>(r[j] - kBiasBits) >> 4;
+          for (uint32_t j = 0; j < C::kCols; j += 2) {
+            acc[j / 2] = f32x2_fma(f32x2_pack(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), s2,
+                                   acc[j / 2]);
+          }
+          if (p.partials != nullptr && n_valid) {
+#pragma unroll
+            for (uint32_t j = 0; j < C::kCols; ++j) {
+              const uint32_t m = w.m0 + col0 + j;
+              if (m < p.M) {
+                p.partials[(size_t(m) * p.N + n) * p.G + g] =
+                    static_cast<int32_t>(r[j] - kBiasBits) >> 4;
+              }
             }
           }
+          bias_sum += s_g * kBiasF;  // exact: 8 significant bits times 2
         }
+        // Both accumulators of the pair are read and re-armed: hand them back.
         tmem_st_wait();
         tc_fence_before_sync();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&s.tmem_empty[acc_b]);
-        if (et == 0 && gi - 8u < 8u) probe_mark(16 + gi - 8u);
-        bias_sum += s_g * kBiasF;  // exact: 8 significant bits times 2
-        if ((g - w.g_begin) % kBiasFlush == kBiasFlush - 1u || g + 1 == w.g_end) {
+        if (lane == 0) mbar_arrive(&s.tmem_empty[pair]);
+        if (et == 0 && si - 4u < 8u) probe_mark(16 + si - 4u);
+        if ((t * kGps) % kBiasFlush == kBiasFlush - kGps || t + 1 == steps_per_tile) {
           const uint64_t nb = f32x2_pack(-bias_sum, -bias_sum);
 #pragma unroll
           for (uint32_t j = 0; j < kPairs; ++j) acc[j] = f32x2_add(acc[j], nb);
           bias_sum = 0.f;
         }
-        if (et == 0 && gi - 8u < 8u) probe_mark(48 + gi - 8u);
+        if (et == 0 && si - 4u < 8u) probe_mark(48 + si - 4u);
       }
       if (!ok) break;
 

@@ -171,6 +171,39 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// Non-blocking test of a phase (acquire when it reports completion). On B200 even a
+// test of an already-completed phase takes ~180 cycles to answer, so code that
+// checks several barriers issues all the tests first and lets their latencies
+// overlap, then blocks (mbar_wait) only on the ones that were not complete.
+__device__ __forceinline__ uint32_t mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok;
+}
+
+// Warp-wide bounded wait on up to two barriers whose completion lane 0 may already
+// have seen (`pre1`, `pre2` from earlier mbar_test calls; pass 1 for "no wait").
+// Lane 0 blocks only on the barriers not yet seen, and the outcome is broadcast.
+// Every lane of the warp must call it (it ends in a full-warp shuffle).
+__device__ __forceinline__ bool mbar_wait_warp2(uint64_t* bar1, uint32_t parity1, uint32_t pre1,
+                                                uint64_t* bar2, uint32_t parity2, uint32_t pre2,
+                                                volatile uint32_t* abort, uint32_t err_bit) {
+  uint32_t ok = 1;
+  if ((threadIdx.x & 31u) == 0u) {
+    ok = ((pre1 != 0u || mbar_wait(bar1, parity1, abort, err_bit)) &&
+          (pre2 != 0u || mbar_wait(bar2, parity2, abort, err_bit)))
+             ? 1u
+             : 0u;
+  }
+  return __shfl_sync(0xffffffffu, ok, 0) != 0u;
+}
+
 // Warp-wide bounded wait: lane 0 waits and the outcome is broadcast, so the warp
 // leaves together. Every lane of the warp must call it (it ends in a full-warp
 // shuffle), never from inside a branch that splits the warp.
