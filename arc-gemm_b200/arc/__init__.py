@@ -6,19 +6,23 @@ the GEMM path is what this package covers):
 * `matmul(a, b, out=None)`            bf16 NT GEMM (drop-in for arc/mm.py:71)
 * `a8w4_matmul((x, sa), (wp, sb), out=None)`  int8 x int4 GEMM with group-128 scales
 * `a8w4_gemm_nt(a, b, out, recipe_a, recipe_b)`  the same with deep_gemm's call shape
+* `quantize_int8(x)`                  bf16 activations -> (int8, per-token fp32 scale) on the GPU
+* `a8w4_matmul_bf16(x, (wp, sb))`     quantize_int8 followed by the A8W4 GEMM
 * `quant`, `math`, `parallel`, `testing` helpers
 
 The kernels are AOT-built into libarcb200.so for sm_100a (`python -m arc.build`).
 """
 from . import math, parallel, quant
 from ._lib import ArcError, describe_plan, device_status, version
-from .a8w4 import a8w4_gemm_nt, a8w4_matmul
+from .a8w4 import a8w4_gemm_nt, a8w4_matmul, a8w4_matmul_bf16, quantize_int8
 from .mm import matmul
 
 __all__ = [
     "matmul",
     "a8w4_matmul",
     "a8w4_gemm_nt",
+    "a8w4_matmul_bf16",
+    "quantize_int8",
     "ArcError",
     "describe_plan",
     "device_status",

@@ -54,6 +54,7 @@ SIGNATURES = {
     "arc_a8w4_describe_plan": ([_I, _I, _I, _I, ctypes.POINTER(Plan)], _I),
     "arc_device_status": ([_I, ctypes.POINTER(ctypes.c_uint32), _I], _I),
     "arc_probe_attach": ([_P, ctypes.c_size_t], _I),
+    "arc_quantize_int8": ([_P, _P, _P, _I, _I, _I, _I, _P], _I),
 }
 
 

@@ -98,3 +98,43 @@ def a8w4_gemm_nt(a: TensorPair, b: TensorPair, out: torch.Tensor,
     if tuple(recipe_b) != (1, GROUP_K):
         raise ValueError(f"recipe_b must be (1, {GROUP_K}), got {tuple(recipe_b)}")
     return a8w4_matmul(a, b, out, group=GROUP_K)
+
+
+def quantize_int8(x: torch.Tensor, out: TensorPair | None = None) -> TensorPair:
+    """bf16 activations [M, K] -> (int8 [M, K], fp32 per-token scale [M]) on the GPU.
+
+    The same numbers as arc.quant.per_token_cast_to_int8 (the host quantizer, which
+    follows the reference's per-token cast, arc/testing/quant.py:30-48), computed by
+    `arc_quantize_int8` on the caller's stream. `out` may supply the (q, sa) buffers.
+    """
+    if not isinstance(x, torch.Tensor) or x.dim() != 2:
+        raise ValueError("quantize_int8 expects a 2D tensor")
+    if x.device.type != "cuda":
+        raise ValueError(f"x must be a CUDA tensor (there is no CPU path), got {x.device}")
+    if x.dtype != torch.bfloat16:
+        raise TypeError(f"x must be torch.bfloat16, got {x.dtype}")
+    if x.stride(1) != 1:
+        raise ValueError("x must have unit stride along K")
+    m, k = x.shape
+    dev = x.device
+    if out is None:
+        q = torch.empty((m, k), dtype=torch.int8, device=dev)
+        sa = torch.empty((m,), dtype=torch.float32, device=dev)
+    else:
+        q, sa = out
+        _expect(q, "out[0]", torch.int8, (m, k), dev)
+        _expect(sa, "out[1]", torch.float32, (m,), dev)
+    with torch.cuda.device(dev):
+        check(lib().arc_quantize_int8(x.data_ptr(), q.data_ptr(), sa.data_ptr(), m, k, x.stride(0),
+                                      q.stride(0), _stream_ptr(dev)),
+              "arc.quantize_int8")
+    return q, sa
+
+
+def a8w4_matmul_bf16(x: torch.Tensor, b: TensorPair, out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 activations through the whole A8W4 path: GPU quantisation, then the GEMM.
+
+    Both kernels run on the caller's stream; the GEMM's prologue overlaps the
+    quantizer (programmatic dependent launch) and reads (q, sa) only after it ends.
+    """
+    return a8w4_matmul(quantize_int8(x), b, out)

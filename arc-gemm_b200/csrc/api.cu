@@ -15,6 +15,7 @@
 #include "arc_b200.h"
 #include "gemm_a8w4.cuh"
 #include "gemm_a8w4_decode.cuh"
+#include "quantize.cuh"
 #include "gemm_bf16.cuh"
 #include "sm100.cuh"
 
@@ -580,6 +581,40 @@ int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uin
                   a8w4_smem_bytes<128, 2, 3>(), 1, stream);
   }
   if (e != cudaSuccess) return cuda_fail(e, "gemm_a8w4_kernel launch");
+  return ARC_OK;
+}
+
+int arc_quantize_int8(const void* x, int8_t* q, float* sa, int M, int K, int ldx, int ldq,
+                      cudaStream_t stream) {
+  g_last_error[0] = '\0';
+  if (x == nullptr || q == nullptr || sa == nullptr) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_quantize_int8: null pointer");
+  }
+  if (M <= 0 || K <= 0 || ldx < K || ldq < K) {
+    return fail(ARC_ERR_INVALID_ARGUMENT,
+                "arc_quantize_int8: need M, K >= 1, ldx >= K, ldq >= K (M=%d K=%d ldx=%d ldq=%d)", M,
+                K, ldx, ldq);
+  }
+  if ((reinterpret_cast<uintptr_t>(x) & 1u) || (reinterpret_cast<uintptr_t>(sa) & 3u)) {
+    return fail(ARC_ERR_UNSUPPORTED, "arc_quantize_int8: x must be 2-byte and sa 4-byte aligned");
+  }
+  int dev = 0;
+  if (int st = current_device(&dev)) return st;
+  arcb::quant::Params p;
+  p.x = static_cast<const uint16_t*>(x);
+  p.q = q;
+  p.sa = sa;
+  p.M = static_cast<uint32_t>(M);
+  p.K = static_cast<uint32_t>(K);
+  p.ldx = static_cast<uint32_t>(ldx);
+  p.ldq = static_cast<uint32_t>(ldq);
+  p.vec = (K % 8 == 0 && ldx % 8 == 0 && ldq % 8 == 0 && aligned16(x) &&
+           (reinterpret_cast<uintptr_t>(q) & 7u) == 0u)
+              ? 1u
+              : 0u;
+  const cudaError_t e = launch_ex(arcb::quant::quantize_int8_per_token_kernel, p,
+                                  static_cast<uint32_t>(M), arcb::quant::kThreads, 0, 1, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "quantize_int8_per_token_kernel launch");
   return ARC_OK;
 }
 

@@ -103,6 +103,21 @@ typedef struct arc_a8w4_plan {
 int arc_a8w4_describe_plan(int M, int N, int K, int num_sms, arc_a8w4_plan_t *plan);
 
 /*
+ * Per-token int8 quantisation of bf16 activations, the producer of the A8W4 GEMM's
+ * activation operand:
+ *   amax[m] = max(max_k |x[m,k]|, 1e-4),  sa[m] = amax[m] / 127  (fp32),
+ *   q[m,k]  = clamp(round_half_even(x[m,k] / sa[m]), -127, 127)  (int8).
+ * Replaces the role of the reference's per-token activation cast
+ * (arc/testing/quant.py:30-48, per_token_cast_to_fp8) for the int8 recipe; results
+ * equal the host quantizer arc.quant.per_token_cast_to_int8 bit for bit.
+ *   x  [M][ldx] bf16 (uint16 storage), q [M][ldq] int8, sa [M] fp32.
+ * Requirements: M, K >= 1; ldx, ldq >= K; x 2-byte and sa 4-byte aligned (16-byte
+ * aligned rows with K, ldx, ldq multiples of 8 take the vector path).
+ */
+int arc_quantize_int8(const void *x, int8_t *q, float *sa, int M, int K, int ldx, int ldq,
+                      cudaStream_t stream);
+
+/*
  * Probe builds only (libarcb200_probe.so, compiled with -DARC_PROBE and loaded by the
  * Python package when the ARC_PROBE environment variable is set). Attaches a device
  * buffer of at least 64 uint64 per CTA; every kernel launched afterwards on the

@@ -60,6 +60,10 @@ def test_invalid_arguments_are_rejected_before_any_cuda_call(native_lib):
         _lib.ARC_ERR_INVALID_ARGUMENT
     # misaligned operand
     assert L.arc_a8w4_gemm(p + 1, p, p, p, p, 16, 64, 256, 128, nul, nul) == _lib.ARC_ERR_UNSUPPORTED
+    # quantizer: null output, leading dimension below K, misaligned input
+    assert L.arc_quantize_int8(p, nul, p, 4, 64, 64, 64, nul) == _lib.ARC_ERR_INVALID_ARGUMENT
+    assert L.arc_quantize_int8(p, p, p, 4, 64, 32, 64, nul) == _lib.ARC_ERR_INVALID_ARGUMENT
+    assert L.arc_quantize_int8(p + 1, p, p, 4, 64, 64, 64, nul) == _lib.ARC_ERR_UNSUPPORTED
 
 
 @pytest.mark.parametrize("m,n,k,expect", [
