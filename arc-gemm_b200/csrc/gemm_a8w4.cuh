@@ -350,13 +350,12 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
     while (ok && next_work<BT>(p, cursor, w)) {
       for (uint32_t t = 0; t < steps_per_tile; ++t, ++si) {
         // Packed tile landed, and the UMMAs that read w[us] last time have retired
-        // (both tested at once by lane 0).
-        uint32_t t1 = 1u, t2 = 1u;
-        if (lane == 0) {
-          t1 = mbar_test(&s.load_full[stage], phase);
-          if (si >= kUnpacked) t2 = mbar_test(&s.mma_done[(si - kUnpacked) % kDoneRing], done_parity(si - kUnpacked));
-        }
-        if (!mbar_wait_warp2(&s.load_full[stage], phase, t1,
+        // (both tested at once).
+        const uint32_t t1 = mbar_test(&s.load_full[stage], phase);
+        const uint32_t t2 = si >= kUnpacked ? mbar_test(&s.mma_done[(si - kUnpacked) % kDoneRing],
+                                                        done_parity(si - kUnpacked))
+                                            : 1u;
+        if (!mbar_wait_all2(&s.load_full[stage], phase, t1,
                              &s.mma_done[(si - kUnpacked) % kDoneRing], done_parity(si - kUnpacked), t2,
                              abort, kStatusTimeoutUnpack)) {
           ok = false;
@@ -416,7 +415,7 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
     const bool vec_sb = (p.G % 8u == 0u) && (p.ldsb % 8u == 0u) &&
                         ((reinterpret_cast<uintptr_t>(p.sb) & 15u) == 0u);
     uint32_t si = 0, cursor = 0;
-    uint32_t pre = 0;  // lane 0: step si's partials seen complete by an early test
+    uint32_t pre = 0;  // step si's partials seen complete by an early test
     Work w;
     bool ok = true;
     while (ok && next_work<BT>(p, cursor, w)) {
@@ -444,7 +443,7 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
       }
       for (uint32_t t = 0; t < steps_per_tile; ++t, ++si) {
         const uint32_t pair = si % kAccPairs;
-        if (!mbar_wait_warp2(&s.mma_done[si % kDoneRing], done_parity(si), pre,
+        if (!mbar_wait_all2(&s.mma_done[si % kDoneRing], done_parity(si), pre,
                              &s.mma_done[si % kDoneRing], done_parity(si), 1u, abort,
                              kStatusTimeoutEpilogue)) {
           ok = false;
@@ -484,7 +483,7 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
           }
           // Ask early whether the next step's partials are ready; the answer arrives
           // while the loads are in flight.
-          if (h == 0 && lane == 0) pre = mbar_test(&s.mma_done[(si + 1u) % kDoneRing], done_parity(si + 1u));
+          if (h == 0) pre = mbar_test(&s.mma_done[(si + 1u) % kDoneRing], done_parity(si + 1u));
           tmem_ld_wait();
 #pragma unroll
           for (uint32_t c = 0; c < C::kCols; c += 8) tmem_st_32x32b_x8_fill(t_row + c, kBiasBits);

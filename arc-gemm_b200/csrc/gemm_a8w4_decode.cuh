@@ -157,24 +157,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) probe_mark(0);  // kernel entry
   pdl_launch_dependents();
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&p.tm_tok);
-    tma_prefetch_desc(&p.tm_wp);
-    tma_prefetch_desc(&p.tm_out);
-    for (uint32_t i = 0; i < p.stages; ++i) {
+  if (warp == 0) {
+    // The ~90 barrier inits are spread over the warp's lanes (each is a shared-memory
+    // operation with a long latency).
+    if (lane == 0) {
+      tma_prefetch_desc(&p.tm_tok);
+      tma_prefetch_desc(&p.tm_wp);
+      tma_prefetch_desc(&p.tm_out);
+    }
+    for (uint32_t i = lane; i < p.stages; i += 32) {
       mbar_init(&s.load_full[i], 1);
       mbar_init(&s.load_empty[i], kUnpackWarps + 1);  // each unpack warp + the UMMA commit
       mbar_init(&s.unpacked[i], kUnpackWarps);
     }
-    for (uint32_t i = 0; i < C::kTmemSlots; ++i) {
+    for (uint32_t i = lane; i < C::kTmemSlots; i += 32) {
       mbar_init(&s.mma_done[i], 1);
       mbar_init(&s.tmem_empty[i], epi_warps);
     }
-    mbar_init(&s.drain, 1);
-    mbar_init(&s.recv_full, 1);
-    s.abort = 0;
+    if (lane == 0) {
+      mbar_init(&s.drain, 1);
+      mbar_init(&s.recv_full, 1);
+      s.abort = 0;
+    }
     fence_barrier_init();
-    if (p.S > 1) {
+    __syncwarp();
+    if (lane == 0 && p.S > 1) {
       // Armed before the cluster barrier below, so every peer's bulk copy lands on a
       // barrier that already expects it.
       mbar_arrive_expect_tx(&s.recv_full, (p.S - 1) * (p.R / p.S) * BT * 4u);
@@ -241,8 +248,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (uint32_t idx = 0; ok && get_item(p, idx, it); ++idx) {
         for (uint32_t g0 = it.g0; ok && g0 < it.g1; g0 += p.gps, ++q) {
-          if (!mbar_wait(&s.load_full[st], st_ph, abort, kStatusTimeoutMma) ||
-              !mbar_wait(&s.unpacked[st], st_ph, abort, kStatusTimeoutMma)) {
+          // Both tested at once (a test costs ~180 cycles even when complete).
+          const uint32_t t_ld = mbar_test(&s.load_full[st], st_ph);
+          const uint32_t t_up = mbar_test(&s.unpacked[st], st_ph);
+          if ((t_ld == 0u && !mbar_wait(&s.load_full[st], st_ph, abort, kStatusTimeoutMma)) ||
+              (t_up == 0u && !mbar_wait(&s.unpacked[st], st_ph, abort, kStatusTimeoutMma))) {
             ok = false;
             break;
           }
@@ -252,7 +262,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t n_in = min(p.gps, it.g1 - g0);
 #pragma unroll 1
           for (uint32_t j = 0; j < n_in; ++j, ++i) {
-            if (!mbar_wait(&s.tmem_empty[ts], ts_ph ^ 1u, abort, kStatusTimeoutMma)) {
+            // A TMEM slot is waited for only when it has been used before.
+            if (i >= C::kTmemSlots &&
+                !mbar_wait(&s.tmem_empty[ts], ts_ph ^ 1u, abort, kStatusTimeoutMma)) {
               ok = false;
               break;
             }

@@ -187,31 +187,18 @@ __device__ __forceinline__ uint32_t mbar_test(uint64_t* bar, uint32_t parity) {
   return ok;
 }
 
-// Warp-wide bounded wait on up to two barriers whose completion lane 0 may already
-// have seen (`pre1`, `pre2` from earlier mbar_test calls; pass 1 for "no wait").
-// Lane 0 blocks only on the barriers not yet seen, and the outcome is broadcast.
-// Every lane of the warp must call it (it ends in a full-warp shuffle).
-__device__ __forceinline__ bool mbar_wait_warp2(uint64_t* bar1, uint32_t parity1, uint32_t pre1,
-                                                uint64_t* bar2, uint32_t parity2, uint32_t pre2,
-                                                volatile uint32_t* abort, uint32_t err_bit) {
-  uint32_t ok = 1;
-  if ((threadIdx.x & 31u) == 0u) {
-    ok = ((pre1 != 0u || mbar_wait(bar1, parity1, abort, err_bit)) &&
-          (pre2 != 0u || mbar_wait(bar2, parity2, abort, err_bit)))
-             ? 1u
-             : 0u;
-  }
-  return __shfl_sync(0xffffffffu, ok, 0) != 0u;
-}
-
-// Warp-wide bounded wait: lane 0 waits and the outcome is broadcast, so the warp
-// leaves together. Every lane of the warp must call it (it ends in a full-warp
-// shuffle), never from inside a branch that splits the warp.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity,
+// Warp-wide bounded wait on up to two barriers. Every lane tests and waits for
+// itself (each lane's wait is its own acquire), skipping a barrier whose completion
+// it already saw in an earlier mbar_test (`pre1`, `pre2`; pass 1 for "no wait"),
+// and the warp leaves together through a vote. On B200 this is measurably faster
+// than one lane waiting and broadcasting the outcome. Every lane of the warp must
+// call it, never from inside a branch that splits the warp.
+__device__ __forceinline__ bool mbar_wait_all2(uint64_t* bar1, uint32_t parity1, uint32_t pre1,
+                                               uint64_t* bar2, uint32_t parity2, uint32_t pre2,
                                                volatile uint32_t* abort, uint32_t err_bit) {
-  uint32_t ok = 0;
-  if ((threadIdx.x & 31u) == 0u) ok = mbar_wait(bar, parity, abort, err_bit) ? 1u : 0u;
-  return __shfl_sync(0xffffffffu, ok, 0) != 0u;
+  const bool ok = (pre1 != 0u || mbar_wait(bar1, parity1, abort, err_bit)) &&
+                  (pre2 != 0u || mbar_wait(bar2, parity2, abort, err_bit));
+  return __all_sync(0xffffffffu, ok);
 }
 
 // Per-warpgroup register budget moves (all four warps of a warpgroup execute the
