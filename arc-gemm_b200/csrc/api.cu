@@ -555,7 +555,7 @@ int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uin
     return st;
   }
   if (int st = encode_2d(&p.tm_wp, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Wp, K / 2, N, K / 2,
-                         Q::kPackedRow * Q::kGps, R, CU_TENSOR_MAP_SWIZZLE_NONE, "Wp")) {
+                         Q::kPackedRow * Q::kGps, R, CU_TENSOR_MAP_SWIZZLE_128B, "Wp")) {
     return st;
   }
   p.sa = sa;

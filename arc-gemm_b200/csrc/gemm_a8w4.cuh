@@ -83,7 +83,7 @@ static_assert(kBiasFlush % kGps == 0, "flush on step boundaries");
 
 struct Params {
   CUtensorMap tm_tok;  // A  [M][K] u8 view of int8, box {128, BT}, SW128
-  CUtensorMap tm_wp;   // Wp [N][K/2] u8, box {128, 128} (two groups), no swizzle
+  CUtensorMap tm_wp;   // Wp [N][K/2] u8, box {128, 128} (two groups), SW128
   const float* sa;
   const uint16_t* sb;
   uint16_t* out;
@@ -125,7 +125,7 @@ struct alignas(1024) Smem {
   using C = Cfg<BT, EWG, LS>;
   uint8_t w[kUnpacked][kGps][C::kWBytes];       // unpacked int8, SW128 (UMMA A)
   uint8_t tok[LS][kGps][C::kTokBytes];          // tokens, SW128 (UMMA B)
-  uint8_t wp[LS][C::kWpBytes];                  // packed int4 [128 rows][2 groups x 64 B]
+  uint8_t wp[LS][C::kWpBytes];                  // packed int4 [128 rows][2 x 64 B], SW128
   uint64_t load_full[LS];                       // TMA bytes landed (tokens + packed W)
   uint64_t w_full[kUnpacked];                   // 4 unpack warps wrote w[u]
   uint64_t mma_done[kDoneRing];                 // the UMMAs of step si retired
@@ -338,12 +338,15 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
     if constexpr (C::kSplitRegs) regs_release<C::kRegsLow>();
     const uint32_t ut = threadIdx.x - 128;  // 0..127
     uint32_t stage = 0, phase = 0, us = 0, si = 0, cursor = 0;
-    // Each warp waits for itself (no warpgroup barrier per step). Per group h of a
-    // step, thread ut converts 16-byte chunks id = i*128 + ut (i < 4) of the packed
-    // tile: row r = id / 4, packed bytes [64h + 16c, +16) with c = id % 4, which become
-    // the 32 int8 bytes [32c, 32c+32) of row r = swizzled 16-byte chunks 2c and 2c+1.
-    // Reads: a warp covers 8 rows x 64 contiguous bytes. Writes: a quarter-warp
-    // covers two rows whose chunk sets {2c ^ (r&7)} are the even and the odd chunks.
+    // Each warp waits for itself (no warpgroup barrier per step). The packed stage is
+    // [128 rows][kGps x 64 B], landed by TMA with the 128-byte swizzle (16-byte chunk
+    // j of row r at position j ^ (r & 7)). Load i of thread ut covers chunk id =
+    // i*128 + ut: group h = id / 512, row r = (id % 512) / 4, K quarter c = id % 4,
+    // i.e. 32 codes that become swizzled int8 chunks 2c and 2c+1 of row r of unpacked
+    // tile h. A quarter-warp handles two consecutive rows of one group: its loads hit
+    // 8 distinct chunk positions and its stores the even and the odd chunks of the
+    // two rows, so neither has bank conflicts.
+    static_assert(kGps == 2, "unpack lane mapping assumes two groups per step");
     const uint32_t c16 = ut & 3u;
     Work w;
     bool ok = true;
@@ -363,30 +366,21 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
         }
         if (ut == 0 && si - 4u < 8u) probe_mark(24 + si - 4u);
         const uint8_t* src = s.wp[stage];
-        uint4 x[kGps][4];
+        uint4 x[8];
 #pragma unroll
-        for (uint32_t h = 0; h < kGps; ++h) {
-#pragma unroll
-          for (uint32_t i = 0; i < 4; ++i) {
-            const uint32_t id = i * 128u + ut;
-            x[h][i] = *reinterpret_cast<const uint4*>(src + (id >> 2) * (kGps * kPackedRow) +
-                                                      h * kPackedRow + c16 * 16u);
-          }
+        for (uint32_t i = 0; i < 8; ++i) {
+          const uint32_t r = (i & 3u) * 32u + (ut >> 2), j = (i >> 2) * 4u + c16;
+          x[i] = *reinterpret_cast<const uint4*>(src + r * (kGps * kPackedRow) + ((j ^ (r & 7u)) << 4));
         }
 #pragma unroll
-        for (uint32_t h = 0; h < kGps; ++h) {
-          uint8_t* dst = s.w[us][h];
-#pragma unroll
-          for (uint32_t i = 0; i < 4; ++i) {
-            const uint32_t r = (i * 128u + ut) >> 2;
-            const uint2 a = expand_int4x8(x[h][i].x), b = expand_int4x8(x[h][i].y);
-            const uint2 c = expand_int4x8(x[h][i].z), d = expand_int4x8(x[h][i].w);
-            uint8_t* row = dst + r * kGroupK;
-            *reinterpret_cast<uint4*>(row + (((2u * c16) ^ (r & 7u)) << 4)) =
-                make_uint4(a.x, a.y, b.x, b.y);
-            *reinterpret_cast<uint4*>(row + (((2u * c16 + 1u) ^ (r & 7u)) << 4)) =
-                make_uint4(c.x, c.y, d.x, d.y);
-          }
+        for (uint32_t i = 0; i < 8; ++i) {
+          const uint32_t r = (i & 3u) * 32u + (ut >> 2);
+          const uint2 a = expand_int4x8(x[i].x), b = expand_int4x8(x[i].y);
+          const uint2 c = expand_int4x8(x[i].z), d = expand_int4x8(x[i].w);
+          uint8_t* row = s.w[us][i >> 2] + r * kGroupK;
+          *reinterpret_cast<uint4*>(row + (((2u * c16) ^ (r & 7u)) << 4)) = make_uint4(a.x, a.y, b.x, b.y);
+          *reinterpret_cast<uint4*>(row + (((2u * c16 + 1u) ^ (r & 7u)) << 4)) =
+              make_uint4(c.x, c.y, d.x, d.y);
         }
         fence_proxy_async_smem();
         __syncwarp();
