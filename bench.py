@@ -336,8 +336,14 @@ def run_ours(args, wl, world, rank, local):
                         call(sets[i % n_sets])
                 graph.replay()  # one untimed replay
                 torch.cuda.synchronize()
-            # Bring clocks to a steady state before the timed region (untimed).
-            t_end = time.time() + args.settle_s
+            # Bring clocks to a steady state before the timed region (untimed). With a
+            # collective in the step every rank must run the same number of steps, so
+            # that case settles for a fixed count instead of a wall-clock time.
+            if gather:
+                for i in range(int(args.settle_s * 2000)):
+                    call(sets[i % n_sets])
+                torch.cuda.synchronize()
+            t_end = time.time() + (0.0 if gather else args.settle_s)
             while time.time() < t_end:
                 if graph is not None:
                     graph.replay()

@@ -1,0 +1,77 @@
+"""Two GPUs: column-sharded A8W4 GEMM with the NCCL all-gather of the output.
+
+Each rank owns half of the weight columns (arc.parallel.shard_weights), runs the CUDA
+GEMM on its slice and all-gathers the bf16 output over NCCL. The gathered result must
+equal the single-GPU GEMM of the whole weight matrix bit for bit (the columns are
+independent, so sharding changes no arithmetic). Skipped with fewer than 2 GPUs.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, m, n, k, result_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    sys.path[:0] = [str(root / "arc-gemm_b200"), str(root)]
+    import arc
+    from arc import parallel as par
+    from arc.testing.data import generate_a8w4
+
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        (x, sa), (wp, sb) = generate_a8w4(m, n, k, seed=5)
+        a = (x.to(dev), sa.to(dev))
+        b_local = par.shard_weights((wp.to(dev), sb.to(dev)), rank, world)
+        full = par.sharded_gemm(arc.a8w4_matmul, a, b_local, world=world, all_gather=True)
+        torch.cuda.synchronize()
+        ref = arc.a8w4_matmul(a, (wp.to(dev), sb.to(dev))) if rank == 0 else None
+        torch.cuda.synchronize()
+        if rank == 0:
+            result_q.put(bool(torch.equal(full, ref)))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("m,n,k", [(16, 4096, 4096), (200, 1024, 1024)])
+def test_two_gpu_sharded_gemm_with_all_gather(m, n, k):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, m, n, k, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        ok = q.get(timeout=240)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    assert ok, "sharded + gathered output differs from the single-GPU GEMM"
+    assert all(p.exitcode == 0 for p in procs)
