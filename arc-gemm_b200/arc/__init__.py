@@ -8,13 +8,15 @@ the GEMM path is what this package covers):
 * `a8w4_gemm_nt(a, b, out, recipe_a, recipe_b)`  the same with deep_gemm's call shape
 * `quantize_int8(x)`                  bf16 activations -> (int8, per-token fp32 scale) on the GPU
 * `a8w4_matmul_bf16(x, (wp, sb))`     quantize_int8 followed by the A8W4 GEMM
+* `fp8_fp4_gemm_nt(a, b, out, recipe_a, recipe_b)`  FP8 x FP4 with UE8M0 block scales, the
+  recipe and call shape of the reference's own A8W4 test
 * `quant`, `math`, `parallel`, `testing` helpers
 
 The kernels are AOT-built into libarcb200.so for sm_100a (`python -m arc.build`).
 """
 from . import math, parallel, quant
 from ._lib import ArcError, describe_plan, device_status, version
-from .a8w4 import a8w4_gemm_nt, a8w4_matmul, a8w4_matmul_bf16, quantize_int8
+from .a8w4 import a8w4_gemm_nt, a8w4_matmul, a8w4_matmul_bf16, fp8_fp4_gemm_nt, quantize_int8
 from .mm import matmul
 
 __all__ = [
@@ -22,6 +24,7 @@ __all__ = [
     "a8w4_matmul",
     "a8w4_gemm_nt",
     "a8w4_matmul_bf16",
+    "fp8_fp4_gemm_nt",
     "quantize_int8",
     "ArcError",
     "describe_plan",

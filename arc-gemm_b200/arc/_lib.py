@@ -55,6 +55,7 @@ SIGNATURES = {
     "arc_device_status": ([_I, ctypes.POINTER(ctypes.c_uint32), _I], _I),
     "arc_probe_attach": ([_P, ctypes.c_size_t], _I),
     "arc_quantize_int8": ([_P, _P, _P, _I, _I, _I, _I, _P], _I),
+    "arc_fp8_fp4_gemm": ([_P, _P, _P, _P, _P, _I, _I, _I, _P], _I),
 }
 
 

@@ -138,3 +138,36 @@ def a8w4_matmul_bf16(x: torch.Tensor, b: TensorPair, out: torch.Tensor | None = 
     quantizer (programmatic dependent launch) and reads (q, sa) only after it ends.
     """
     return a8w4_matmul(quantize_int8(x), b, out)
+
+
+def fp8_fp4_gemm_nt(a: TensorPair, b: TensorPair, out: torch.Tensor,
+                    recipe_a: Sequence[int] = (1, 128), recipe_b: Sequence[int] = (1, 32)) -> torch.Tensor:
+    """FP8 x FP4 GEMM with UE8M0 block scales: the call shape of the reference's A8W4 test.
+
+    The reference calls `deep_gemm.fp8_fp4_gemm_nt(a, b, out, recipe_a=(1, 128),
+    recipe_b=(1, 32))` (tests/a8w4.py:48, :70) with
+        a = (x  float8_e4m3fn [M, K], sfa float32 [M, K/128])  (powers of two)
+        b = (wp uint8 [N, K/2] packed e2m1,  sfw float32 [N, K/32])
+    and a preallocated bf16 `out` [M, N]; this runs `arc_fp8_fp4_gemm` on the same
+    tensors (block-scaled tcgen05 MMA, fp32 accumulation).
+    """
+    if tuple(recipe_a) != (1, 128) or tuple(recipe_b) != (1, 32):
+        raise ValueError(f"supported recipes: recipe_a=(1, 128), recipe_b=(1, 32); got "
+                         f"{tuple(recipe_a)}, {tuple(recipe_b)}")
+    x, sfa = a
+    wp, sfw = b
+    m, k = x.shape
+    n, k2 = wp.shape
+    assert k == 2 * k2, f"Inner dimensions must match: {k} vs 2*{k2}"
+    assert k % 128 == 0, f"K ({k}) must be a multiple of 128"
+    dev = x.device
+    _expect(x, "a[0]", torch.float8_e4m3fn, (m, k), None)
+    _expect(sfa, "a[1]", torch.float32, (m, k // 128), dev)
+    _expect(wp, "b[0]", torch.uint8, (n, k // 2), dev)
+    _expect(sfw, "b[1]", torch.float32, (n, k // 32), dev)
+    _expect(out, "out", torch.bfloat16, (m, n), dev)
+    with torch.cuda.device(dev):
+        check(lib().arc_fp8_fp4_gemm(x.data_ptr(), sfa.data_ptr(), wp.data_ptr(), sfw.data_ptr(),
+                                     out.data_ptr(), m, n, k, _stream_ptr(dev)),
+              "arc.fp8_fp4_gemm_nt")
+    return out

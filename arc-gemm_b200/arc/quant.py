@@ -86,3 +86,77 @@ __all__ = [
     "per_group_cast_to_int4",
     "dequantize_int4",
 ]
+
+
+# ------------------------------------------------------------------ FP8 x FP4 recipe
+# The quantisation of the reference's A8W4 test (tests/a8w4.py:29-30): e4m3
+# activations with one power-of-two (UE8M0) scale per token and 128-wide K block, e2m1
+# weights with one per row and 32-wide K block. Restated from
+# arc/testing/quant.py:16-19 (ceil_to_ue8m0), :30-48 (per_token_cast_to_fp8),
+# :51-58 (e2m1 rounding), :61-84 (per_token_cast_to_fp4) and arc/math.py:148-170
+# (the e2m1 decode used by cast_back_from_fp4).
+FP8_E4M3_MAX = 448.0
+FP4_E2M1_MAX = 6.0
+E2M1_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
+_E2M1_EDGES = (0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0)  # rounding boundaries between values
+
+
+def ceil_to_ue8m0(s: torch.Tensor) -> torch.Tensor:
+    """Smallest power of two >= |s| (biased exponent clamped to [1, 254]), as fp32."""
+    bits = s.abs().float().view(torch.int32)
+    exp = ((bits >> 23) & 0xFF) + ((bits & 0x7FFFFF) != 0).to(torch.int32)
+    return (exp.clamp(1, 254) << 23).view(torch.float32)
+
+
+def _blocks(x: torch.Tensor, gran_k: int) -> torch.Tensor:
+    """[M, K] -> zero-padded [M, ceil(K/gran_k), gran_k] view."""
+    m, k = x.shape
+    kp = -(-k // gran_k) * gran_k
+    xp = torch.zeros((m, kp), dtype=x.dtype, device=x.device)
+    xp[:, :k] = x
+    return xp.view(m, kp // gran_k, gran_k)
+
+
+def per_token_cast_to_fp8(x: torch.Tensor, *, use_ue8m0: bool = True, gran_k: int = 128) -> TensorPair:
+    """x [M, K] -> (float8_e4m3fn [M, K], fp32 scale [M, ceil(K/gran_k)])."""
+    if x.dim() != 2:
+        raise ValueError("per-token fp8 casting expects a 2D tensor")
+    view = _blocks(x, gran_k)
+    sf = view.abs().float().amax(dim=2).clamp(1e-4) / FP8_E4M3_MAX
+    if use_ue8m0:
+        sf = ceil_to_ue8m0(sf)
+    q = (view * (1.0 / sf.unsqueeze(2))).to(torch.float8_e4m3fn)
+    return q.view(x.shape[0], -1)[:, : x.shape[1]].contiguous(), sf
+
+
+def _round_to_e2m1(v: torch.Tensor) -> torch.Tensor:
+    """fp32 -> e2m1 code (magnitude index 0..7, bit 3 = sign, no negative zero)."""
+    edges = torch.tensor(_E2M1_EDGES, dtype=torch.float32, device=v.device)
+    idx = torch.bucketize(v.abs().clamp_max(FP4_E2M1_MAX).float(), edges)
+    neg = (v < 0) & (idx != 0)
+    return idx.to(torch.uint8) | (neg.to(torch.uint8) << 3)
+
+
+def per_token_cast_to_fp4(x: torch.Tensor, *, use_ue8m0: bool = True, gran_k: int = 32) -> TensorPair:
+    """x [N, K] -> (packed e2m1 uint8 [N, K/2], fp32 scale [N, ceil(K/gran_k)])."""
+    if x.dim() != 2:
+        raise ValueError("per-token fp4 casting expects a 2D tensor")
+    if x.shape[1] % 2 != 0:
+        raise ValueError("packed fp4 casting expects an even K")
+    view = _blocks(x, gran_k)
+    sf = view.abs().float().amax(dim=2).clamp_min(1e-4) / FP4_E2M1_MAX
+    if use_ue8m0:
+        sf = ceil_to_ue8m0(sf)
+    codes = _round_to_e2m1(view * (1.0 / sf.unsqueeze(2))).view(x.shape[0], -1)
+    packed = codes[:, 0::2] | (codes[:, 1::2] << 4)
+    return packed[:, : x.shape[1] // 2].contiguous(), sf
+
+
+def dequantize_fp4(packed: torch.Tensor, sf: torch.Tensor, gran_k: int = 32) -> torch.Tensor:
+    """(packed e2m1 [N, K/2], fp32 scale [N, K/gran_k]) -> fp32 [N, K]."""
+    p = packed.to(torch.uint8)
+    codes = torch.stack((p & 0x0F, p >> 4), dim=-1).flatten(-2)
+    table = torch.tensor(E2M1_VALUES, dtype=torch.float32, device=p.device)
+    mag = table[(codes & 0x07).long()]
+    val = torch.where((codes & 0x08) != 0, -mag, mag)
+    return val * sf.float().repeat_interleave(gran_k, dim=1)[:, : val.shape[1]]

@@ -15,6 +15,7 @@
 #include "arc_b200.h"
 #include "gemm_a8w4.cuh"
 #include "gemm_a8w4_decode.cuh"
+#include "gemm_fp8fp4.cuh"
 #include "quantize.cuh"
 #include "gemm_bf16.cuh"
 #include "sm100.cuh"
@@ -181,6 +182,9 @@ int init_device(int dev) {
     }
     if (e == cudaSuccess) {
       e = allow_smem(arcb::a8w4dec::gemm_a8w4_decode_kernel<32>, decode_smem_bytes<32>());
+    }
+    if (e == cudaSuccess) {
+      e = allow_smem(arcb::fp8fp4::gemm_fp8fp4_kernel, sizeof(arcb::fp8fp4::Smem) + 1024);
     }
     if (e != cudaSuccess) {
       st.status = cuda_fail(e, "cudaFuncSetAttribute");
@@ -581,6 +585,59 @@ int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uin
                   a8w4_smem_bytes<128, 2, 3>(), 1, stream);
   }
   if (e != cudaSuccess) return cuda_fail(e, "gemm_a8w4_kernel launch");
+  return ARC_OK;
+}
+
+int arc_fp8_fp4_gemm(const uint8_t* A, const float* sfa, const uint8_t* Wp, const float* sfw,
+                     uint16_t* C, int M, int N, int K, cudaStream_t stream) {
+  g_last_error[0] = '\0';
+  if (A == nullptr || sfa == nullptr || Wp == nullptr || sfw == nullptr || C == nullptr) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_fp8_fp4_gemm: null pointer");
+  }
+  if (M <= 0 || N <= 0 || K <= 0) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_fp8_fp4_gemm: sizes must be positive (M=%d N=%d K=%d)",
+                M, N, K);
+  }
+  if (K % 128 != 0 || N % 8 != 0) {
+    return fail(ARC_ERR_UNSUPPORTED, "arc_fp8_fp4_gemm: need K %% 128 == 0 and N %% 8 == 0 (N=%d K=%d)",
+                N, K);
+  }
+  if (!aligned16(A) || !aligned16(Wp) || !aligned16(C) || !aligned16(sfw) ||
+      (reinterpret_cast<uintptr_t>(sfa) & 3u)) {
+    return fail(ARC_ERR_UNSUPPORTED,
+                "arc_fp8_fp4_gemm: A, Wp, C and sfw must be 16-byte aligned (sfa 4-byte)");
+  }
+  int dev = 0;
+  if (int st = current_device(&dev)) return st;
+  namespace F = arcb::fp8fp4;
+  F::Params p;
+  if (int st = encode_2d(&p.tm_tok, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, K, M, K, F::kGroupK, F::kBT,
+                         CU_TENSOR_MAP_SWIZZLE_128B, "A")) {
+    return st;
+  }
+  if (int st = encode_2d(&p.tm_wp, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Wp, K / 2, N, K / 2,
+                         F::kPackedRow * F::kGps, F::kRows, CU_TENSOR_MAP_SWIZZLE_128B, "Wp")) {
+    return st;
+  }
+  p.sfa = sfa;
+  p.sfw = sfw;
+  p.out = C;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.G = static_cast<uint32_t>(K) / F::kGroupK;
+  p.ldsfa = static_cast<uint32_t>(K) / 128u;
+  p.ldsfw = static_cast<uint32_t>(K) / 32u;
+  p.ldc = N;
+  p.R = F::kRows;
+  p.tiles_m = ceil_div(M, F::kBT);
+  p.tiles_n = ceil_div(N, F::kRows);
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  const uint32_t sms = static_cast<uint32_t>(g_dev[dev].sms);
+  const uint32_t grid = p.num_tiles < sms ? p.num_tiles : sms;
+  const cudaError_t e = launch_ex(F::gemm_fp8fp4_kernel, p, grid, F::kThreads,
+                                  sizeof(F::Smem) + 1024, 1, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm_fp8fp4_kernel launch");
   return ARC_OK;
 }
 

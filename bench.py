@@ -50,6 +50,9 @@ WORKLOADS = {
     "prefill": dict(kind="a8w4", M=4096, N=14336, K=4096),
     "bf16_2048": dict(kind="bf16", M=2048, N=2048, K=2048),
     "bf16_8192": dict(kind="bf16", M=8192, N=8192, K=8192),
+    # The recipe of the reference's own A8W4 test: e4m3 x e2m1 with UE8M0 block scales.
+    "fp8fp4_prefill": dict(kind="fp8fp4", M=4096, N=14336, K=4096),
+    "fp8fp4_decode": dict(kind="fp8fp4", M=16, N=4096, K=4096),
 }
 
 
@@ -59,6 +62,10 @@ def a8w4_bytes(M, N, K, group=128):
 
 def bf16_bytes(M, N, K):
     return 2 * (M * K + N * K + M * N)
+
+
+def fp8fp4_bytes(M, N, K):
+    return M * K + 4 * M * (K // 128) + N * K // 2 + 4 * N * (K // 32) + 2 * M * N
 
 
 def load_peaks():
@@ -257,6 +264,10 @@ def config_of(args, wl, world):
     if wl["kind"] == "a8w4":
         cfg.update(group=128, activations="int8 + fp32 per-token scale",
                    weights="int4 packed x2 + bf16 per-(column,128) scale")
+    elif wl["kind"] == "fp8fp4":
+        cfg.update(recipe_a="(1, 128)", recipe_b="(1, 32)",
+                   activations="e4m3 + UE8M0 scale per (token, 128-K block)",
+                   weights="e2m1 packed x2 + UE8M0 scale per (row, 32-K block)")
     return cfg
 
 
@@ -272,6 +283,15 @@ def build_inputs(wl, rank, device, n_sets):
             (x, sa), (wp, sb) = generate_a8w4(wl["M"], wl["N"], wl["K"], seed=seed)
             out = torch.empty((wl["M"], wl["N"]), dtype=torch.bfloat16, device=device)
             sets.append(((x.to(device), sa.to(device)), (wp.to(device), sb.to(device)), out))
+        elif wl["kind"] == "fp8fp4":
+            from arc import quant
+
+            g = torch.Generator(device=device).manual_seed(seed)
+            a = torch.randn(wl["M"], wl["K"], generator=g, device=device, dtype=torch.bfloat16)
+            b = torch.randn(wl["N"], wl["K"], generator=g, device=device, dtype=torch.bfloat16)
+            out = torch.empty((wl["M"], wl["N"]), dtype=torch.bfloat16, device=device)
+            sets.append((quant.per_token_cast_to_fp8(a, use_ue8m0=True, gran_k=128),
+                         quant.per_token_cast_to_fp4(b, use_ue8m0=True, gran_k=32), out))
         else:
             a, b = generate_bf16(wl["M"], wl["N"], wl["K"], seed=seed, device=device)
             out = torch.empty((wl["M"], wl["N"]), dtype=torch.bfloat16, device=device)
@@ -293,6 +313,12 @@ def run_ours(args, wl, world, rank, local):
 
         def call(s):
             return arc.a8w4_matmul(s[0], s[1], s[2])
+    elif wl["kind"] == "fp8fp4":
+        step_bytes = fp8fp4_bytes(M, N, K)
+        in_bytes = step_bytes - 2 * M * N
+
+        def call(s):
+            return arc.fp8_fp4_gemm_nt(s[0], s[1], s[2], recipe_a=(1, 128), recipe_b=(1, 32))
     else:
         step_bytes = bf16_bytes(M, N, K)
         in_bytes = step_bytes - 2 * M * N
@@ -392,7 +418,7 @@ def run_ours(args, wl, world, rank, local):
     if rank != 0:
         return
     value = world * ops / (step_ms * 1e-3) / 1e12
-    if wl["kind"] == "a8w4":
+    if wl["kind"] in ("a8w4", "fp8fp4"):
         bound = "hbm" if M <= 128 else "tensor"
     else:
         bound = "tensor"
@@ -405,18 +431,24 @@ def run_ours(args, wl, world, rank, local):
         if wl["kind"] == "a8w4":
             peak = 2.0 * peaks["bf16_tflops"]  # kind::i8 issues at twice the kind::f16 rate
             peak_note = f"2 x bf16_tflops ({peaks['source']}): dense int8 = 2x dense bf16"
+        elif wl["kind"] == "fp8fp4":
+            peak = 2.0 * peaks["bf16_tflops"]  # kind::mxf8f6f4 (e4m3 operands) = int8 rate
+            peak_note = f"2 x bf16_tflops ({peaks['source']}): dense fp8 = 2x dense bf16"
         else:
             peak = peaks["bf16_tflops"]
             peak_note = f"bf16_tflops ({peaks['source']})"
         unit = "TOPS" if wl["kind"] == "a8w4" else "TFLOP/s"
     traffic = traffic_from_profiles(args.workload)
     line = {
-        "metric": "A8W4 GEMM TOPS & HBM GB/s vs roofline, M in {16,4096}, 1/2/4/8 B200"
-                  if wl["kind"] == "a8w4" else "bf16 GEMM TFLOP/s vs roofline",
+        "metric": {"a8w4": "A8W4 GEMM TOPS & HBM GB/s vs roofline, M in {16,4096}, 1/2/4/8 B200",
+                   "fp8fp4": "FP8xFP4 (UE8M0 block scales) GEMM TFLOP/s vs roofline"}.get(
+                       wl["kind"], "bf16 GEMM TFLOP/s vs roofline"),
         "value": value, "unit": "TOPS" if wl["kind"] == "a8w4" else "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8xint4->int32, fp32 scale, bf16 out" if wl["kind"] == "a8w4" else "bf16",
+        "dtype": {"a8w4": "int8xint4->int32, fp32 scale, bf16 out",
+                  "fp8fp4": "e4m3 x e2m1, UE8M0 block scales, fp32 accumulate, bf16 out"}.get(
+                      wl["kind"], "bf16"),
         "data": "synthetic (seeded, BASELINE distributions)",
         "config": dict(config_of(args, wl, world),
                        l2=("rotating %d distinct input sets (%.0f MB) > L2" %
@@ -430,7 +462,8 @@ def run_ours(args, wl, world, rank, local):
                      "frac": achieved / peak, "traffic": traffic,
                      "peak_source": peak_note,
                      "algorithmic_per_launch": step_bytes if bound == "hbm" else ops,
-                     "kernel": "gemm_a8w4_kernel" if wl["kind"] == "a8w4" else "gemm_bf16_kernel"},
+                     "kernel": {"a8w4": "gemm_a8w4_kernel", "fp8fp4": "gemm_fp8fp4_kernel"}.get(
+                         wl["kind"], "gemm_bf16_kernel")},
         "e2e": {"value": world * ops / (e2e_ms * 1e-3) / 1e12,
                 "unit": "TOPS" if wl["kind"] == "a8w4" else "TFLOP/s",
                 "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
@@ -453,16 +486,20 @@ def run_e2e(args, wl, s, device, stream, world):
 
     import arc
 
-    if wl["kind"] == "a8w4":
+    if wl["kind"] in ("a8w4", "fp8fp4"):
         (x, sa), (wp, sb), _ = s
         host = [t.cpu().pin_memory() for t in (x, sa, wp, sb)]
         dev_bufs = [torch.empty_like(t) for t in (x, sa, wp, sb)]
         out_h = torch.empty((wl["M"], wl["N"]), dtype=torch.bfloat16).pin_memory()
+        out_d = torch.empty((wl["M"], wl["N"]), dtype=torch.bfloat16, device=device)
 
         def step():
             for h, d in zip(host, dev_bufs):
                 d.copy_(h, non_blocking=True)
-            o = arc.a8w4_matmul((dev_bufs[0], dev_bufs[1]), (dev_bufs[2], dev_bufs[3]))
+            if wl["kind"] == "a8w4":
+                o = arc.a8w4_matmul((dev_bufs[0], dev_bufs[1]), (dev_bufs[2], dev_bufs[3]))
+            else:
+                o = arc.fp8_fp4_gemm_nt((dev_bufs[0], dev_bufs[1]), (dev_bufs[2], dev_bufs[3]), out_d)
             out_h.copy_(o, non_blocking=True)
     else:
         a, b, _ = s

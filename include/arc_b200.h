@@ -103,6 +103,22 @@ typedef struct arc_a8w4_plan {
 int arc_a8w4_describe_plan(int M, int N, int K, int num_sms, arc_a8w4_plan_t *plan);
 
 /*
+ * FP8 x FP4 GEMM with UE8M0 block scales, the recipe of the reference's A8W4 test
+ * (tests/a8w4.py:29-30 quantisation, :48 the deep_gemm.fp8_fp4_gemm_nt call with
+ * recipe_a = (1, 128), recipe_b = (1, 32)):
+ *   C[m,n] = bf16( sum_k A[m,k] sfa[m,k/128] * W[n,k] sfw[n,k/32] )   (fp32 accumulate)
+ *   A    [M][K]      float8 e4m3 (uint8 storage), contiguous
+ *   sfa  [M][K/128]  fp32 powers of two (UE8M0 values)
+ *   Wp   [N][K/2]    uint8, two e2m1 codes per byte (magnitude index | sign << 3), the even
+ *                    k in the low nibble (arc/testing/quant.py:51-84)
+ *   sfw  [N][K/32]   fp32 powers of two
+ *   C    [M][N]      bf16 (uint16 storage)
+ * Requirements: K % 128 == 0; N % 8 == 0; M, N >= 1; A, Wp, C, sfw 16-byte aligned.
+ */
+int arc_fp8_fp4_gemm(const uint8_t *A, const float *sfa, const uint8_t *Wp, const float *sfw,
+                     uint16_t *C, int M, int N, int K, cudaStream_t stream);
+
+/*
  * Per-token int8 quantisation of bf16 activations, the producer of the A8W4 GEMM's
  * activation operand:
  *   amax[m] = max(max_k |x[m,k]|, 1e-4),  sa[m] = amax[m] / 127  (fp32),

@@ -144,6 +144,44 @@ def np_a8w4_partials(a: np.ndarray, w_packed: np.ndarray, group: int = 128) -> n
     return P.astype(np.int32)
 
 
+# ------------------------------------------------------------ FP8 x FP4 (UE8M0 blocks)
+def e4m3_to_f64(bits: np.ndarray) -> np.ndarray:
+    """float8 e4m3 (fn) bytes -> float64: sign bit 7, 4-bit exponent (bias 7), 3-bit
+    mantissa, subnormals at exponent 0, 0x7F / 0xFF NaN (no infinities)."""
+    b = np.asarray(bits, np.uint8).astype(np.int64)
+    sign = np.where(b & 0x80, -1.0, 1.0)
+    e = (b >> 3) & 0xF
+    m = b & 0x7
+    val = np.where(e == 0, m / 8.0 * 2.0 ** -6, (1.0 + m / 8.0) * np.ldexp(1.0, e - 7))
+    val = np.where((b & 0x7F) == 0x7F, np.nan, val)
+    return sign * val
+
+
+E2M1 = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])
+
+
+def e2m1_unpack_f64(packed: np.ndarray) -> np.ndarray:
+    """[N, K/2] packed e2m1 (even k in the low nibble; code = magnitude | sign << 3,
+    arc/testing/quant.py:51-84, decoded as arc/math.py:148-153) -> float64 [N, K]."""
+    p = np.asarray(packed, np.uint8)
+    codes = np.empty((p.shape[0], p.shape[1] * 2), np.uint8)
+    codes[:, 0::2] = p & 0x0F
+    codes[:, 1::2] = p >> 4
+    mag = E2M1[codes & 7]
+    return np.where(codes & 8, -mag, mag)
+
+
+def fp8fp4_out(x_bits, sfa, w_packed, sfw) -> np.ndarray:
+    """out[m,n] = sum_k x[m,k] sfa[m,k/128] * w[n,k] sfw[n,k/32] in float64 (every
+    product of the scaled operands is exact; only the sum's order differs from the
+    tensor core's)."""
+    a = e4m3_to_f64(x_bits)
+    k = a.shape[1]
+    a = a * np.repeat(np.asarray(sfa, np.float64), 128, axis=1)[:, :k]
+    w = e2m1_unpack_f64(w_packed) * np.repeat(np.asarray(sfw, np.float64), 32, axis=1)[:, :k]
+    return a @ w.T
+
+
 # ----------------------------------------------------------------------- parity metric
 def bf16_ulp(x: np.ndarray) -> np.ndarray:
     """Spacing of bf16 numbers at |x| (normal range; subnormals get the min spacing)."""

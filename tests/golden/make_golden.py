@@ -16,6 +16,9 @@ Fixtures:
   fp4 grid point, so the packer's codes are known in advance.
 * ref_metric_pin.npz — the reference's symm_square_rel_L2_error (arc/math.py:14-23)
   and count_bytes (arc/math.py:26-33) on seeded inputs.
+* ref_fp8fp4_pin.npz — the reference's FP8 / FP4 quantizers (arc/testing/quant.py:30-84,
+  the recipe of tests/a8w4.py:29-30) on seeded bf16 inputs, and its fp4 decode
+  (arc/math.py:159-170): pins arc.quant's ports of them bit for bit.
 * a8w4_small.npz / bf16_small.npz — small seeded GEMM cases with the oracle's exact
   partials and float64 outputs; the partials are cross-checked here against an
   independent numpy formulation before being written.
@@ -86,6 +89,23 @@ def metric_pin(ref_math):
                         symm=np.array(vals), zero=np.array(zero_val), count_bytes=np.array(nbytes))
 
 
+def fp8fp4_pin(ref_math, ref_quant):
+    g = torch.Generator().manual_seed(31)
+    a = torch.randn(12, 384, generator=g).to(torch.bfloat16)
+    b = torch.randn(20, 384, generator=g).to(torch.bfloat16)
+    b[3, :40] = 0  # an all-zero block (scale clamp) and ties at block edges
+    b[4, 5] = 3.0 * 2 ** -3
+    xq, sfa = ref_quant.per_token_cast_to_fp8(a, use_ue8m0=True, gran_k=128)
+    wq, sfw = ref_quant.per_token_cast_to_fp4(b, use_ue8m0=True, gran_k=32)
+    back = ref_math.cast_back_from_fp4(wq, sfw, gran_k=32)
+    np.savez_compressed(HERE / "ref_fp8fp4_pin.npz",
+                        a=a.view(torch.int16).numpy().view(np.uint16),
+                        b=b.view(torch.int16).numpy().view(np.uint16),
+                        xq=xq.view(torch.uint8).numpy(), sfa=sfa.numpy(),
+                        wq=wq.view(torch.uint8).numpy(), sfw=sfw.numpy(),
+                        dequant=back.float().numpy())
+
+
 def a8w4_small():
     from arc.testing.data import generate_a8w4
     from oracle import oracle
@@ -125,6 +145,7 @@ def main():
     ref_math, ref_quant = _reference()
     nibble_pin(ref_math, ref_quant)
     metric_pin(ref_math)
+    fp8fp4_pin(ref_math, ref_quant)
     # Drop the reference package from sys.modules so the local `arc` imports cleanly.
     for name in [m for m in sys.modules if m == "arc" or m.startswith("arc.")]:
         del sys.modules[name]
