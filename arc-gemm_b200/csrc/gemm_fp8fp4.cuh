@@ -45,8 +45,8 @@ using a8w4::kUmmaK;
 using a8w4::Work;
 
 constexpr uint32_t kGps = 2;        // K-groups per pipeline step
-constexpr uint32_t kUnpacked = 3;   // unpacked weight stages (steps)
-constexpr uint32_t kLoadStages = 2;
+constexpr uint32_t kUnpacked = 2;   // unpacked weight stages (steps)
+constexpr uint32_t kLoadStages = 3;
 constexpr uint32_t kDoneRing = 8;
 constexpr uint32_t kBT = 128;       // tokens per tile (UMMA N)
 constexpr uint32_t kSfCol = 2 * kBT;  // first TMEM column of the scale-factor slots
@@ -72,8 +72,10 @@ struct alignas(1024) Smem {
   uint64_t load_full[kLoadStages];
   uint64_t w_full[kUnpacked];
   uint64_t mma_done[kDoneRing];
+  uint32_t xch[2][kGps][2][kRows];                  // scale words, [step parity][group][A/B][row]
   uint64_t tile_full[2];
   uint64_t tmem_empty[2];
+  uint64_t xch_full[2];                             // 4 unpack warps wrote xch[b]
   uint32_t tmem_base;
   uint32_t abort;
 };
@@ -152,6 +154,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8fp4_kernel(const __grid_c
   volatile uint32_t* abort = &s.abort;
   const uint32_t steps_per_tile = (p.G + kGps - 1) / kGps;
 
+  // Probe stamps (probe build only), steps 4..11: 0-7 UMMAs issued, 8-15 unpack waits
+  // passed, 16-23 stage unpacked, 24-31 loads issued; 32-35 tiles 0..3 drained by the
+  // epilogue; 56 entry, 57 prologue done.
+  if (threadIdx.x == 0) probe_mark(56);
   pdl_launch_dependents();
   if (warp == 0) {
     if (lane == 0) {
@@ -164,6 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8fp4_kernel(const __grid_c
     for (uint32_t i = lane; i < 2; i += 32) {
       mbar_init(&s.tile_full[i], 1);
       mbar_init(&s.tmem_empty[i], 8);  // the 8 epilogue warps
+      mbar_init(&s.xch_full[i], 4);    // the 4 unpack warps
     }
     if (lane == 0) s.abort = 0;
     fence_barrier_init();
@@ -177,6 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8fp4_kernel(const __grid_c
   tc_fence_after_sync();
   const uint32_t tmem_base = s.tmem_base;
   pdl_wait();
+  if (threadIdx.x == 0) probe_mark(57);
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -194,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8fp4_kernel(const __grid_c
           }
           const uint32_t g0 = w.g_begin + t * kGps;
           const uint32_t real = min(kGps, w.g_end - g0);
+          if (si - 4u < 8u) probe_mark(24 + si - 4u);
           mbar_arrive_expect_tx(&s.load_full[stage], real * kBT * kGroupK + kRows * kPackedRow * kGps);
 #pragma unroll
           for (uint32_t h = 0; h < kGps; ++h) {
@@ -248,6 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8fp4_kernel(const __grid_c
             }
           }
           umma_commit(&s.mma_done[si % kDoneRing]);
+          if (si - 4u < 8u) probe_mark(si - 4u);
           if (++stage == kLoadStages) {
             stage = 0;
             phase ^= 1u;
@@ -268,32 +278,59 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8fp4_kernel(const __grid_c
     const uint32_t ut = threadIdx.x - 128;  // 0..127 = this thread's TMEM lane
     const uint32_t lane_addr = ((ut & ~31u) << 16);
     const uint32_t c16 = ut & 3u;
-    uint32_t stage = 0, phase = 0, us = 0, si = 0, cursor = 0;
+    uint32_t stage = 0, phase = 0, us = 0, si = 0;
     Work w;
     bool ok = true;
     const uint32_t r0 = ut & 31u;
-    while (ok && next_tile(p, cursor, w)) {
-      for (uint32_t t = 0; t < steps_per_tile; ++t, ++si) {
-        // Scale words of this step's groups for rows r0 + 32c (loaded before the wait,
-        // consumed after it).
-        uint32_t wa[kGps][4], wb[kGps][4];
+    // Scale words. The TMEM layout needs, in every lane quarter, lane r0 holding the
+    // words of rows r0 + 32c (c = 0..3). Each thread loads only its own row ut (weights:
+    // 32 contiguous bytes; tokens: two floats), one step ahead of use; the four warps
+    // then trade words through s.xch, guarded by the bounded mbarrier xch_full.
+    struct Sf {
+      uint32_t wa[kGps], wb[kGps];
+    };
+    auto load_sf = [&](const Work& ww, uint32_t tt, Sf& f) {
+      const uint32_t n = ww.n0 + ut, m = ww.m0 + ut;
+      const uint32_t g0 = ww.g_begin + tt * kGps;
+#pragma unroll
+      for (uint32_t h = 0; h < kGps; ++h) {
+        const uint32_t g = g0 + h;
+        f.wa[h] = 0x7F7F7F7Fu;
+        f.wb[h] = 0x7F7F7F7Fu;
+        if (g < ww.g_end) {
+          if (n < p.N) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(p.sfw + size_t(n) * p.ldsfw) + g);
+            f.wa[h] = ue8m0(v.x) | (ue8m0(v.y) << 8) | (ue8m0(v.z) << 16) | (ue8m0(v.w) << 24);
+          }
+          if (m < p.M) f.wb[h] = ue8m0(__ldg(p.sfa + size_t(m) * p.ldsfa + g)) * 0x01010101u;
+        }
+      }
+    };
+    Work wn;
+    uint32_t cursor_n = 0, tn = 0;
+    bool have = next_tile(p, cursor_n, wn);
+    Sf cur, nxt;
+    if (have) load_sf(wn, 0, cur);
+    while (ok && have) {
+      w = wn;
+      for (uint32_t t = 0; t < steps_per_tile; ++t) {
+        // Publish this step's words of row ut.
+        const uint32_t xb = si & 1u;
 #pragma unroll
         for (uint32_t h = 0; h < kGps; ++h) {
-          const uint32_t g = w.g_begin + t * kGps + h;
-#pragma unroll
-          for (uint32_t c = 0; c < 4; ++c) {
-            const uint32_t n = w.n0 + r0 + 32u * c, m = w.m0 + r0 + 32u * c;
-            wa[h][c] = 0x7F7F7F7Fu;
-            wb[h][c] = 0x7F7F7F7Fu;
-            if (g < w.g_end) {
-              if (n < p.N) {
-                const float4 f = __ldg(reinterpret_cast<const float4*>(p.sfw + size_t(n) * p.ldsfw) + g);
-                wa[h][c] = ue8m0(f.x) | (ue8m0(f.y) << 8) | (ue8m0(f.z) << 16) | (ue8m0(f.w) << 24);
-              }
-              if (m < p.M) wb[h][c] = ue8m0(__ldg(p.sfa + size_t(m) * p.ldsfa + g)) * 0x01010101u;
-            }
-          }
+          s.xch[xb][h][0][ut] = cur.wa[h];
+          s.xch[xb][h][1][ut] = cur.wb[h];
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.xch_full[xb]);
+        // Position of the next step (possibly in the next tile) and its scales.
+        tn = t + 1;
+        bool more = true;
+        if (tn == steps_per_tile) {
+          tn = 0;
+          more = next_tile(p, cursor_n, wn);
+        }
+        if (more) load_sf(tn == 0 ? wn : w, tn, nxt);
         const uint32_t t1 = mbar_test(&s.load_full[stage], phase);
         const uint32_t t2 = si >= kUnpacked ? mbar_test(&s.mma_done[(si - kUnpacked) % kDoneRing],
                                                         done_parity(si - kUnpacked))
@@ -303,6 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8fp4_kernel(const __grid_c
           ok = false;
           break;
         }
+        if (ut == 0 && si - 4u < 8u) probe_mark(8 + si - 4u);
         tc_fence_after_sync();
         // Same lane mapping as the int8 kernel's unpack (conflict-free with the
         // 128-byte swizzle of the packed tile).
@@ -322,21 +360,40 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8fp4_kernel(const __grid_c
           *reinterpret_cast<uint4*>(row + (((2u * c16) ^ (r & 7u)) << 4)) = lo;
           *reinterpret_cast<uint4*>(row + (((2u * c16 + 1u) ^ (r & 7u)) << 4)) = hi;
         }
+        // The four warps' words of this step: lane r0 takes rows r0 + 32c.
+        if (!mbar_wait_all2(&s.xch_full[xb], (si >> 1) & 1u, 0u, &s.xch_full[xb], 0u, 1u, abort,
+                            kStatusTimeoutUnpack)) {
+          ok = false;
+          break;
+        }
 #pragma unroll
         for (uint32_t h = 0; h < kGps; ++h) {
-          tmem_st_32x32b_x4(tmem_base + lane_addr + sf_col(us, h), wa[h]);
-          tmem_st_32x32b_x4(tmem_base + lane_addr + sf_col(us, h) + 4u, wb[h]);
+          uint32_t va[4], vb[4];
+#pragma unroll
+          for (uint32_t c = 0; c < 4; ++c) {
+            va[c] = s.xch[xb][h][0][r0 + 32u * c];
+            vb[c] = s.xch[xb][h][1][r0 + 32u * c];
+          }
+          tmem_st_32x32b_x4(tmem_base + lane_addr + sf_col(us, h), va);
+          tmem_st_32x32b_x4(tmem_base + lane_addr + sf_col(us, h) + 4u, vb);
         }
         tmem_st_wait();
         fence_proxy_async_smem();
         tc_fence_before_sync();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.w_full[us]);
+        if (ut == 0 && si - 4u < 8u) probe_mark(16 + si - 4u);
         if (++stage == kLoadStages) {
           stage = 0;
           phase ^= 1u;
         }
         if (++us == kUnpacked) us = 0;
+        ++si;
+        cur = nxt;
+        if (tn == 0) {
+          have = more;
+          break;  // the tile is done; `wn` holds the next one
+        }
       }
     }
   } else if (warp >= 8) {
@@ -362,6 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8fp4_kernel(const __grid_c
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.tmem_empty[acc]);
+      if (threadIdx.x == 256 && ti < 4u) probe_mark(32 + ti);
       const uint32_t n = w.n0 + nl;
       if (nl < p.R && n < p.N) {
         uint16_t* o = p.out + n;
