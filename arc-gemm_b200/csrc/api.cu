@@ -81,6 +81,30 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t elem_bytes, 
   return ARC_OK;
 }
 
+// Packed e2m1 codes [N][K/2 bytes] viewed as [G][N][128 codes] of type 16U4_ALIGN16B:
+// group g's weight tile is the box {128, rows, groups} at (0, n0, g); in shared memory
+// every 16 codes (8 bytes) are padded to 16 bytes, so a 128-code row takes 128 bytes
+// and the 128-byte swizzle applies as for an 8-bit tile. Needs a 32-byte aligned base
+// and K % 64 == 0 (row stride a multiple of 32 bytes).
+int encode_e2m1_3d(CUtensorMap* map, const void* ptr, uint64_t N, uint64_t K, uint32_t box_rows,
+                   uint32_t box_groups) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(ARC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[3] = {128, N, K / 128};
+  const cuuint64_t strides[2] = {K / 2, 64};
+  const cuuint32_t box[3] = {128, box_rows, box_groups};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<void*>(ptr), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return fail(ARC_ERR_CUDA, "cuTensorMapEncodeTiled(e2m1 weights 3-D) failed with CUresult %d",
+                static_cast<int>(r));
+  }
+  return ARC_OK;
+}
+
 // A [M][K] byte matrix viewed as [G][M][128]: group g's token tile is the 3-D box
 // {128, rows, groups} at (0, m0, g), landing as consecutive [rows][128] tiles.
 int encode_tokens_3d(CUtensorMap* map, const void* ptr, uint64_t M, uint64_t K, uint32_t box_rows,
@@ -184,7 +208,19 @@ int init_device(int dev) {
       e = allow_smem(arcb::a8w4dec::gemm_a8w4_decode_kernel<32>, decode_smem_bytes<32>());
     }
     if (e == cudaSuccess) {
-      e = allow_smem(arcb::fp8fp4::gemm_fp8fp4_kernel, sizeof(arcb::fp8fp4::Smem) + 1024);
+      e = allow_smem(arcb::fp8fp4::gemm_fp8fp4_kernel<1>, sizeof(arcb::fp8fp4::Smem<1>) + 1024);
+    }
+    if (e == cudaSuccess) {
+      e = allow_smem(arcb::fp8fp4::gemm_fp8fp4_kernel<2>, sizeof(arcb::fp8fp4::Smem<2>) + 1024);
+    }
+    if (e == cudaSuccess) {
+      cudaFuncAttributes fa;
+      e = cudaFuncGetAttributes(&fa, arcb::fp8fp4::gemm_fp8fp4_kernel<2>);
+      if (e == cudaSuccess && fa.numRegs != static_cast<int>(arcb::fp8fp4::Cfg<2>::kLaunchRegs)) {
+        st.status = fail(ARC_ERR_UNSUPPORTED,
+                         "gemm_fp8fp4_kernel was compiled with an unexpected register count");
+        return;
+      }
     }
     if (e != cudaSuccess) {
       st.status = cuda_fail(e, "cudaFuncSetAttribute");
@@ -602,23 +638,30 @@ int arc_fp8_fp4_gemm(const uint8_t* A, const float* sfa, const uint8_t* Wp, cons
     return fail(ARC_ERR_UNSUPPORTED, "arc_fp8_fp4_gemm: need K %% 128 == 0 and N %% 8 == 0 (N=%d K=%d)",
                 N, K);
   }
-  if (!aligned16(A) || !aligned16(Wp) || !aligned16(C) || !aligned16(sfw) ||
+  if (!aligned16(A) || (reinterpret_cast<uintptr_t>(Wp) & 31u) || !aligned16(C) || !aligned16(sfw) ||
       (reinterpret_cast<uintptr_t>(sfa) & 3u)) {
     return fail(ARC_ERR_UNSUPPORTED,
-                "arc_fp8_fp4_gemm: A, Wp, C and sfw must be 16-byte aligned (sfa 4-byte)");
+                "arc_fp8_fp4_gemm: A, C and sfw must be 16-byte aligned, Wp 32-byte (sfa 4-byte)");
   }
   int dev = 0;
   if (int st = current_device(&dev)) return st;
   namespace F = arcb::fp8fp4;
+  const uint32_t sms = static_cast<uint32_t>(g_dev[dev].sms);
+  // 256-row weight tiles halve the L2 bytes per MAC; they are used when they still give
+  // every SM a tile, else 128-row tiles (twice the CTAs, e.g. for decode batches).
+  // ARC_FP8FP4_ROWS=128|256 forces one (tests and tuning).
+  uint32_t rows = ceil_div(M, F::kBT) * ceil_div(N, 256) >= sms ? 256u : 128u;
+  if (const char* env = getenv("ARC_FP8FP4_ROWS")) {
+    const int v = atoi(env);
+    if (v != 128 && v != 256) {
+      return fail(ARC_ERR_INVALID_ARGUMENT, "ARC_FP8FP4_ROWS must be 128 or 256 (got '%s')", env);
+    }
+    rows = static_cast<uint32_t>(v);
+  }
   F::Params p;
-  if (int st = encode_2d(&p.tm_tok, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, K, M, K, F::kGroupK, F::kBT,
-                         CU_TENSOR_MAP_SWIZZLE_128B, "A")) {
-    return st;
-  }
-  if (int st = encode_2d(&p.tm_wp, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Wp, K / 2, N, K / 2,
-                         F::kPackedRow * F::kGps, F::kRows, CU_TENSOR_MAP_SWIZZLE_128B, "Wp")) {
-    return st;
-  }
+  const uint32_t gps = rows == 256 ? F::Cfg<2>::kGps : F::Cfg<1>::kGps;
+  if (int st = encode_tokens_3d(&p.tm_tok, A, M, K, F::kBT, gps)) return st;
+  if (int st = encode_e2m1_3d(&p.tm_w, Wp, N, K, rows, gps)) return st;
   p.sfa = sfa;
   p.sfw = sfw;
   p.out = C;
@@ -629,14 +672,13 @@ int arc_fp8_fp4_gemm(const uint8_t* A, const float* sfa, const uint8_t* Wp, cons
   p.ldsfa = static_cast<uint32_t>(K) / 128u;
   p.ldsfw = static_cast<uint32_t>(K) / 32u;
   p.ldc = N;
-  p.R = F::kRows;
   p.tiles_m = ceil_div(M, F::kBT);
-  p.tiles_n = ceil_div(N, F::kRows);
+  p.tiles_n = ceil_div(N, rows);
   p.num_tiles = p.tiles_m * p.tiles_n;
-  const uint32_t sms = static_cast<uint32_t>(g_dev[dev].sms);
   const uint32_t grid = p.num_tiles < sms ? p.num_tiles : sms;
-  const cudaError_t e = launch_ex(F::gemm_fp8fp4_kernel, p, grid, F::kThreads,
-                                  sizeof(F::Smem) + 1024, 1, stream);
+  const cudaError_t e =
+      rows == 256 ? launch_ex(F::gemm_fp8fp4_kernel<2>, p, grid, F::kThreads, sizeof(F::Smem<2>) + 1024, 1, stream)
+                  : launch_ex(F::gemm_fp8fp4_kernel<1>, p, grid, F::kThreads, sizeof(F::Smem<1>) + 1024, 1, stream);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_fp8fp4_kernel launch");
   return ARC_OK;
 }
