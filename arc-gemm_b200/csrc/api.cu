@@ -14,8 +14,10 @@
 
 #include "arc_b200.h"
 #include "gemm_a8w4.cuh"
+#include "gemm_bf16_pair.cuh"
 #include "gemm_a8w4_decode.cuh"
 #include "gemm_fp8fp4.cuh"
+#include "gemm_fp8fp4_pair.cuh"
 #include "quantize.cuh"
 #include "gemm_bf16.cuh"
 #include "sm100.cuh"
@@ -137,6 +139,8 @@ struct DeviceState {
   int sms = 0;
   int max_clusters2 = 0;  // co-resident 2-CTA clusters of the decode kernel
   int max_clusters4 = 0;  // co-resident 4-CTA clusters of the decode kernel
+  int max_bf16_pairs = 0;  // co-resident CTA pairs of the bf16 pair kernel
+  int max_fp8fp4_pairs = 0;  // co-resident CTA pairs of the FP8 x FP4 pair kernel
 };
 DeviceState g_dev[kMaxDevices];
 
@@ -177,6 +181,7 @@ int init_device(int dev) {
     }
     st.sms = prop.multiProcessorCount;
     e = allow_smem(arcb::bf16::gemm_bf16_kernel, arcb::bf16::kSmemBytes);
+    if (e == cudaSuccess) e = allow_smem(arcb::bf16pair::gemm_bf16_pair_kernel, arcb::bf16pair::kSmemBytes);
     // The persistent kernel moves registers between its warpgroups (setmaxnreg); the
     // shares are sized for a launch count of Cfg::kLaunchRegs per thread, and a
     // different compiled count could leave an increase waiting, so refuse it.
@@ -214,6 +219,18 @@ int init_device(int dev) {
       e = allow_smem(arcb::fp8fp4::gemm_fp8fp4_kernel<2>, sizeof(arcb::fp8fp4::Smem<2>) + 1024);
     }
     if (e == cudaSuccess) {
+      e = allow_smem(arcb::fp8fp4pair::gemm_fp8fp4_pair_kernel, arcb::fp8fp4pair::kSmemBytes);
+    }
+    if (e == cudaSuccess) {
+      cudaFuncAttributes fa;
+      e = cudaFuncGetAttributes(&fa, arcb::fp8fp4pair::gemm_fp8fp4_pair_kernel);
+      if (e == cudaSuccess && fa.numRegs != static_cast<int>(arcb::fp8fp4pair::kLaunchRegs)) {
+        st.status = fail(ARC_ERR_UNSUPPORTED,
+                         "gemm_fp8fp4_pair_kernel was compiled with an unexpected register count");
+        return;
+      }
+    }
+    if (e == cudaSuccess) {
       cudaFuncAttributes fa;
       e = cudaFuncGetAttributes(&fa, arcb::fp8fp4::gemm_fp8fp4_kernel<2>);
       if (e == cudaSuccess && fa.numRegs != static_cast<int>(arcb::fp8fp4::Cfg<2>::kLaunchRegs)) {
@@ -246,6 +263,44 @@ int init_device(int dev) {
         n = 0;
       }
       (size == 2 ? st.max_clusters2 : st.max_clusters4) = n;
+    }
+    {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(st.sms, 1, 1);
+      cfg.blockDim = dim3(arcb::bf16pair::kNumThreads, 1, 1);
+      cfg.dynamicSmemBytes = arcb::bf16pair::kSmemBytes;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, arcb::bf16pair::gemm_bf16_pair_kernel, &cfg) != cudaSuccess) {
+        cudaGetLastError();  // clear; bf16 GEMMs then use the one-CTA kernel
+        n = 0;
+      }
+      st.max_bf16_pairs = n;
+    }
+    {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(st.sms, 1, 1);
+      cfg.blockDim = dim3(arcb::fp8fp4pair::kThreads, 1, 1);
+      cfg.dynamicSmemBytes = arcb::fp8fp4pair::kSmemBytes;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, arcb::fp8fp4pair::gemm_fp8fp4_pair_kernel, &cfg) != cudaSuccess) {
+        cudaGetLastError();  // clear; FP8 x FP4 GEMMs then use the one-CTA kernels
+        n = 0;
+      }
+      st.max_fp8fp4_pairs = n;
     }
   });
   if (st.status != ARC_OK) {
@@ -463,6 +518,51 @@ int arc_matmul_bf16(const void* A, const void* B, void* C, int M, int N, int K, 
   }
   int dev = 0;
   if (int st = current_device(&dev)) return st;
+  const uint32_t sms = static_cast<uint32_t>(g_dev[dev].sms);
+  // CTA pairs (256 x 256 tiles, half the shared-memory traffic per MAC) once the pair
+  // tiles fill at least half the SMs; one CTA per 128 x 256 tile below that.
+  // ARC_BF16_CTAS=1|2 forces one (tests and tuning).
+  const uint32_t max_pairs = static_cast<uint32_t>(g_dev[dev].max_bf16_pairs);
+  bool pairs = max_pairs > 0 && static_cast<uint32_t>(ceil_div(M, 256) * ceil_div(N, 256)) * 4 >= sms;
+  if (const char* env = getenv("ARC_BF16_CTAS")) {
+    const int v = atoi(env);
+    if (v != 1 && v != 2) {
+      return fail(ARC_ERR_INVALID_ARGUMENT, "ARC_BF16_CTAS must be 1 or 2 (got '%s')", env);
+    }
+    pairs = v == 2;
+    if (pairs && max_pairs == 0) {
+      return fail(ARC_ERR_UNSUPPORTED, "ARC_BF16_CTAS=2: no CTA pair of the bf16 kernel fits on this device");
+    }
+  }
+  if (pairs) {
+    namespace P2 = arcb::bf16pair;
+    P2::Params p;
+    if (int st = encode_2d(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A, K, M, lda, P2::BK,
+                           P2::kRowsPerCta, CU_TENSOR_MAP_SWIZZLE_128B, "A")) {
+      return st;
+    }
+    if (int st = encode_2d(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, B, K, N, ldb, P2::BK,
+                           P2::kRowsPerCta, CU_TENSOR_MAP_SWIZZLE_128B, "B")) {
+      return st;
+    }
+    if (int st = encode_2d(&p.tm_c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, N, M, ldc,
+                           P2::kEpiCols, P2::kRowsPerCta, CU_TENSOR_MAP_SWIZZLE_64B, "C")) {
+      return st;
+    }
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.tiles_m = ceil_div(M, P2::kTileM);
+    p.tiles_n = ceil_div(N, P2::kTileN);
+    p.num_tiles = p.tiles_m * p.tiles_n;
+    p.num_kb = ceil_div(K, P2::BK);
+    // One wave of co-resident pairs strides over the pair tiles.
+    const uint32_t grid = 2 * (p.num_tiles < max_pairs ? p.num_tiles : max_pairs);
+    const cudaError_t e =
+        launch_ex(P2::gemm_bf16_pair_kernel, p, grid, P2::kNumThreads, P2::kSmemBytes, 2, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "gemm_bf16_pair_kernel launch");
+    return ARC_OK;
+  }
   namespace B16 = arcb::bf16;
   B16::Params p;
   if (int st = encode_2d(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A, K, M, lda, B16::BK,
@@ -484,9 +584,7 @@ int arc_matmul_bf16(const void* A, const void* B, void* C, int M, int N, int K, 
   p.tiles_n = ceil_div(N, B16::BN);
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.num_kb = ceil_div(K, B16::BK);
-  const uint32_t grid = p.num_tiles < static_cast<uint32_t>(g_dev[dev].sms)
-                            ? p.num_tiles
-                            : static_cast<uint32_t>(g_dev[dev].sms);
+  const uint32_t grid = p.num_tiles < sms ? p.num_tiles : sms;
   const cudaError_t e =
       launch_ex(B16::gemm_bf16_kernel, p, grid, B16::kNumThreads, B16::kSmemBytes, 1, stream);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_bf16_kernel launch");
@@ -647,16 +745,54 @@ int arc_fp8_fp4_gemm(const uint8_t* A, const float* sfa, const uint8_t* Wp, cons
   if (int st = current_device(&dev)) return st;
   namespace F = arcb::fp8fp4;
   const uint32_t sms = static_cast<uint32_t>(g_dev[dev].sms);
-  // 256-row weight tiles halve the L2 bytes per MAC; they are used when they still give
-  // every SM a tile, else 128-row tiles (twice the CTAs, e.g. for decode batches).
-  // ARC_FP8FP4_ROWS=128|256 forces one (tests and tuning).
+  // Kernel choice. CTA pairs on 256 x 256 tiles (half the shared-memory bytes per MAC)
+  // when the pair tiles give every pair one and K % 512 == 0 (the token-scale tensor map
+  // needs a 16-byte row pitch); else one CTA per 256-row weight tile when those fill the
+  // SMs; else 128-row tiles (twice the CTAs, e.g. for decode batches).
+  // ARC_FP8FP4_KERNEL=128|256|pair forces one (tests and tuning).
+  const uint32_t max_pairs = static_cast<uint32_t>(g_dev[dev].max_fp8fp4_pairs);
   uint32_t rows = ceil_div(M, F::kBT) * ceil_div(N, 256) >= sms ? 256u : 128u;
-  if (const char* env = getenv("ARC_FP8FP4_ROWS")) {
-    const int v = atoi(env);
-    if (v != 128 && v != 256) {
-      return fail(ARC_ERR_INVALID_ARGUMENT, "ARC_FP8FP4_ROWS must be 128 or 256 (got '%s')", env);
+  const bool pairs_ok = max_pairs > 0 && K % 512 == 0 && aligned16(sfa);
+  bool pairs = pairs_ok && ceil_div(M, 256) * ceil_div(N, 256) >= max_pairs;
+  if (const char* env = getenv("ARC_FP8FP4_KERNEL")) {
+    if (strcmp(env, "pair") == 0) {
+      if (!pairs_ok) {
+        return fail(ARC_ERR_UNSUPPORTED,
+                    "ARC_FP8FP4_KERNEL=pair needs K %% 512 == 0, a 16-byte aligned sfa and a co-resident CTA pair");
+      }
+      pairs = true;
+    } else if (strcmp(env, "128") == 0 || strcmp(env, "256") == 0) {
+      rows = static_cast<uint32_t>(atoi(env));
+      pairs = false;
+    } else {
+      return fail(ARC_ERR_INVALID_ARGUMENT, "ARC_FP8FP4_KERNEL must be 128, 256 or pair (got '%s')", env);
     }
-    rows = static_cast<uint32_t>(v);
+  }
+  if (pairs) {
+    namespace FP = arcb::fp8fp4pair;
+    FP::Params q;
+    if (int st = encode_tokens_3d(&q.tm_tok, A, M, K, 128, 1)) return st;
+    if (int st = encode_e2m1_3d(&q.tm_w, Wp, N, K, 128, 1)) return st;
+    if (int st = encode_2d(&q.tm_sfw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, sfw, K / 32, N, K / 32, 4,
+                           128, CU_TENSOR_MAP_SWIZZLE_NONE, "sfw")) {
+      return st;
+    }
+    if (int st = encode_2d(&q.tm_sfa, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, sfa, K / 128, M, K / 128, 4,
+                           256, CU_TENSOR_MAP_SWIZZLE_NONE, "sfa")) {
+      return st;
+    }
+    q.out = C;
+    q.M = M;
+    q.N = N;
+    q.G = static_cast<uint32_t>(K) / F::kGroupK;
+    q.ldc = N;
+    q.tiles_m = ceil_div(M, FP::kTileT);
+    q.tiles_n = ceil_div(N, FP::kTileW);
+    q.num_tiles = q.tiles_m * q.tiles_n;
+    const uint32_t grid = 2 * (q.num_tiles < max_pairs ? q.num_tiles : max_pairs);
+    const cudaError_t e = launch_ex(FP::gemm_fp8fp4_pair_kernel, q, grid, FP::kThreads, FP::kSmemBytes, 2, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "gemm_fp8fp4_pair_kernel launch");
+    return ARC_OK;
   }
   F::Params p;
   const uint32_t gps = rows == 256 ? F::Cfg<2>::kGps : F::Cfg<1>::kGps;

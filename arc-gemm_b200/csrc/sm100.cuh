@@ -493,6 +493,83 @@ __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, const void* src,
       : "memory");
 }
 
+// ---------------------------------------------------------------------------------
+// CTA pairs (cta_group::2): two CTAs of a 2-CTA cluster share one UMMA. The MMA of
+// M=256 takes A rows 0-127 from rank 0's shared memory and 128-255 from rank 1's (same
+// offset), B's N/2 halves likewise, and writes D rows 0-127 / 128-255 into the TMEM of
+// rank 0 / rank 1. Rank 0 issues it; its completion can be signalled to both CTAs.
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Arrive (release at cluster scope) on an mbarrier given by its shared::cluster address
+// (map_to_rank), possibly in the peer CTA.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+// 2-D tiled load into this CTA's shared memory whose completion is signalled on an
+// mbarrier of either CTA of the pair (`bar` is a shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_t bar, void* dst,
+                                                 int32_t x, int32_t y, uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::"
+      "cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "l"(cache_hint)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(const CUtensorMap* map, uint32_t bar, void* dst, int32_t x,
+                                                 int32_t y, int32_t z, uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::"
+      "cache_hint [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z), "l"(cache_hint)
+      : "memory");
+}
+
+// TMEM allocation shared by the pair: one warp of each CTA (same warp index) executes
+// it with the same destination offset; both CTAs receive the same column base.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// Pair UMMA, bf16 inputs, fp32 accumulation (idesc with M = 256).
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on the mbarrier at `bar`'s offset in every CTA of `cta_mask` when all
+// pair tcgen05 operations issued so far by this thread have completed. (This is the
+// completion signal of tcgen05, not a memory load.)
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
+}
+
 // Programmatic dependent launch: let the next grid in the stream start its
 // prologue, and wait for the previous grid's completion (and memory) before
 // touching global memory.

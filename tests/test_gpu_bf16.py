@@ -2,7 +2,9 @@
 
 Small and ragged shapes are checked against the CPU oracle (float64 of the bf16
 inputs); the BASELINE sizes against an fp32 GPU reference (TF32 off) of the same
-inputs. The bar is 2 bf16 ulps (rtol ~1e-2).
+inputs. The bar is 2 bf16 ulps (rtol ~1e-2). Both kernels run every small shape: the
+one-CTA 128 x 256 tile kernel and the CTA-pair 256 x 256 kernel (ARC_BF16_CTAS forces
+one; large problems pick the pair kernel on their own).
 """
 from __future__ import annotations
 
@@ -21,15 +23,18 @@ def _bits(t: torch.Tensor) -> np.ndarray:
     return t.view(torch.int16).numpy().view(np.uint16)
 
 
+@pytest.mark.parametrize("ctas", [1, 2])
 @pytest.mark.parametrize("m,n,k", [
-    (128, 256, 64),     # exactly one tile, one K block
+    (128, 256, 64),     # exactly one tile, one K block (half a pair tile)
     (32, 128, 128),     # the reference's minimum legal shape
     (1, 8, 8),          # tiny and ragged everywhere
     (200, 264, 320),    # ragged M, N, K
     (384, 768, 1000),   # K tail inside a block
     (1024, 1024, 2048),
+    (300, 520, 192),    # pair tiles whose second CTA holds no rows / columns
 ])
-def test_bf16_vs_oracle(cuda_device, m, n, k):
+def test_bf16_vs_oracle(cuda_device, monkeypatch, m, n, k, ctas):
+    monkeypatch.setenv("ARC_BF16_CTAS", str(ctas))
     a, b = generate_bf16(m, n, k, seed=m + n + k)
     out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=cuda_device)
     arc.matmul(a.to(cuda_device), b.to(cuda_device), out=out)
@@ -62,8 +67,10 @@ def test_bf16_baseline_sizes(cuda_device, m, n, k):
     assert oracle.symm_square_rel_L2_error(out.float().cpu().numpy(), cub) < 1e-5
 
 
-def test_bf16_strided_operands(cuda_device):
+@pytest.mark.parametrize("ctas", [1, 2])
+def test_bf16_strided_operands(cuda_device, monkeypatch, ctas):
     """Row pitch larger than K (a column slice of a wider matrix)."""
+    monkeypatch.setenv("ARC_BF16_CTAS", str(ctas))
     dev = cuda_device
     a_full, b_full = generate_bf16(256, 384, 512, seed=9, device=dev)
     a = a_full[:, :448]
