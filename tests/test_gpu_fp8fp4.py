@@ -30,15 +30,19 @@ def _data(m, n, k, seed):
     return a_ref, b_ref, a, b
 
 
-@pytest.mark.parametrize("rows", [128, 256])
+@pytest.mark.parametrize("kernel", ["128", "256", "pair"])
 @pytest.mark.parametrize("m,n,k", [(128, 128, 128), (16, 256, 512), (200, 136, 384),
-                                   (1, 8, 128), (256, 1024, 4096), (300, 520, 1152)])
-def test_fp8_fp4_gemm_matches_oracle(cuda_device, monkeypatch, m, n, k, rows):
-    """Both weight-tile heights (128 rows, double-buffered accumulators, two K groups
-    per stage; 256 rows, two UMMAs per K step, one accumulator), forced through
-    ARC_FP8FP4_ROWS; the shapes cover ragged M and N, N below one tile, and odd group
-    counts (K = 384, 1152)."""
-    monkeypatch.setenv("ARC_FP8FP4_ROWS", str(rows))
+                                   (1, 8, 128), (256, 1024, 4096), (300, 520, 1152),
+                                   (300, 520, 1024), (520, 264, 2048)])
+def test_fp8_fp4_gemm_matches_oracle(cuda_device, monkeypatch, m, n, k, kernel):
+    """All three kernels, forced through ARC_FP8FP4_KERNEL: 128-row weight tiles
+    (double-buffered accumulators, two K groups per stage), 256-row tiles (two UMMAs per
+    K step), and CTA pairs on 256 x 256 tiles (K % 512 == 0 only). The shapes cover
+    ragged M and N, N below one tile, pair tiles whose second CTA holds no rows, and odd
+    group counts (K = 384, 1152)."""
+    if kernel == "pair" and k % 512:
+        pytest.skip("the pair kernel needs K % 512 == 0")
+    monkeypatch.setenv("ARC_FP8FP4_KERNEL", kernel)
     a_ref, b_ref, (x, sfa), (wp, sfw) = _data(m, n, k, seed=m + n + k)
     dev = cuda_device
     out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=dev)
@@ -49,7 +53,7 @@ def test_fp8_fp4_gemm_matches_oracle(cuda_device, monkeypatch, m, n, k, rows):
     got = out.float().cpu().numpy()
     ref = oracle.fp8fp4_out(x.view(torch.uint8).numpy(), sfa.numpy(), wp.numpy(), sfw.numpy())
     ok, msg = oracle.check_bf16_close(got, ref, max_ulp=2.0, atol=oracle.tensor_core_atol(k, ref))
-    assert ok, f"{m}x{n}x{k} rows={rows}: {msg}"
+    assert ok, f"{m}x{n}x{k} kernel={kernel}: {msg}"
     # The reference's own acceptance test, against the unquantized product.
     full = (a_ref.double() @ b_ref.double().T).numpy()
     assert oracle.symm_square_rel_L2_error(got, full) < 1e-2
