@@ -773,12 +773,12 @@ int arc_fp8_fp4_gemm(const uint8_t* A, const float* sfa, const uint8_t* Wp, cons
     FP::Params q;
     if (int st = encode_tokens_3d(&q.tm_tok, A, M, K, 128, 1)) return st;
     if (int st = encode_e2m1_3d(&q.tm_w, Wp, N, K, 128, 1)) return st;
-    if (int st = encode_2d(&q.tm_sfw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, sfw, K / 32, N, K / 32, 4,
-                           128, CU_TENSOR_MAP_SWIZZLE_NONE, "sfw")) {
+    if (int st = encode_2d(&q.tm_sfw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, sfw, K / 32, N, K / 32,
+                           4 * FP::kBlk, 128, CU_TENSOR_MAP_SWIZZLE_128B, "sfw")) {
       return st;
     }
-    if (int st = encode_2d(&q.tm_sfa, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, sfa, K / 128, M, K / 128, 4,
-                           256, CU_TENSOR_MAP_SWIZZLE_NONE, "sfa")) {
+    if (int st = encode_2d(&q.tm_sfa, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, sfa, K / 128, M, K / 128,
+                           FP::kBlk, 256, CU_TENSOR_MAP_SWIZZLE_NONE, "sfa")) {
       return st;
     }
     q.out = C;
