@@ -15,7 +15,7 @@ the GEMM path is what this package covers):
 The kernels are AOT-built into libarcb200.so for sm_100a (`python -m arc.build`).
 """
 from . import math, parallel, quant
-from ._lib import ArcError, describe_plan, device_status, version
+from ._lib import ArcError, describe_plan, device_status, kernel_name, version
 from .a8w4 import a8w4_gemm_nt, a8w4_matmul, a8w4_matmul_bf16, fp8_fp4_gemm_nt, quantize_int8
 from .mm import matmul
 
@@ -29,6 +29,7 @@ __all__ = [
     "ArcError",
     "describe_plan",
     "device_status",
+    "kernel_name",
     "version",
     "math",
     "parallel",

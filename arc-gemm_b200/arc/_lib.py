@@ -56,7 +56,11 @@ SIGNATURES = {
     "arc_probe_attach": ([_P, ctypes.c_size_t], _I),
     "arc_quantize_int8": ([_P, _P, _P, _I, _I, _I, _I, _P], _I),
     "arc_fp8_fp4_gemm": ([_P, _P, _P, _P, _P, _I, _I, _I, _P], _I),
+    "arc_kernel_name": ([_I, _I, _I, _I, ctypes.c_char_p, _I], _I),
 }
+
+# Operation codes of arc_kernel_name (include/arc_b200.h).
+OP_MATMUL_BF16, OP_A8W4, OP_FP8_FP4 = 0, 1, 2
 
 
 def probe_enabled() -> bool:
@@ -101,6 +105,14 @@ def describe_plan(M: int, N: int, K: int, num_sms: int = 148) -> dict:
     check(lib().arc_a8w4_describe_plan(M, N, K, num_sms, ctypes.byref(plan)),
           "arc_a8w4_describe_plan")
     return plan.as_dict()
+
+
+def kernel_name(op: int, M: int, N: int, K: int) -> str:
+    """Name of the kernel launched for an operation of this shape on the current device
+    (op: OP_MATMUL_BF16, OP_A8W4 or OP_FP8_FP4), as ncu lists it."""
+    buf = ctypes.create_string_buffer(128)
+    check(lib().arc_kernel_name(op, M, N, K, buf, len(buf)), "arc_kernel_name")
+    return buf.value.decode()
 
 
 def device_status(device: int, clear: bool = True) -> int:

@@ -473,6 +473,56 @@ cudaError_t launch_ex(Kern kernel, const P& p, uint32_t grid, uint32_t threads, 
   return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
+// bf16 kernel choice. CTA pairs (256 x 256 tiles, half the shared-memory traffic per
+// MAC) once the pair tiles fill at least half the SMs; one CTA per 128 x 256 tile below
+// that. ARC_BF16_CTAS=1|2 forces one (tests and tuning).
+int choose_bf16(int dev, int M, int N, bool* pairs) {
+  const uint32_t sms = static_cast<uint32_t>(g_dev[dev].sms);
+  const uint32_t max_pairs = static_cast<uint32_t>(g_dev[dev].max_bf16_pairs);
+  *pairs = max_pairs > 0 && static_cast<uint32_t>(ceil_div(M, 256) * ceil_div(N, 256)) * 4 >= sms;
+  if (const char* env = getenv("ARC_BF16_CTAS")) {
+    const int v = atoi(env);
+    if (v != 1 && v != 2) {
+      return fail(ARC_ERR_INVALID_ARGUMENT, "ARC_BF16_CTAS must be 1 or 2 (got '%s')", env);
+    }
+    if (v == 2 && max_pairs == 0) {
+      return fail(ARC_ERR_UNSUPPORTED, "ARC_BF16_CTAS=2: no CTA pair of the bf16 kernel fits on this device");
+    }
+    *pairs = v == 2;
+  }
+  return ARC_OK;
+}
+
+// FP8 x FP4 kernel choice (variant 0: 128-row tiles, 1: 256-row tiles, 2: CTA pairs).
+// Pairs on 256 x 256 tiles (full-rate N=256 UMMAs, half the shared-memory bytes per MAC)
+// when the pair tiles give every co-resident pair one and K % 512 == 0 (the token-scale
+// tensor map needs a 16-byte row pitch); else one CTA per 256-row weight tile when
+// those fill the SMs; else 128-row tiles (twice the CTAs, e.g. for decode batches).
+// ARC_FP8FP4_KERNEL=128|256|pair forces one (tests and tuning).
+int choose_fp8fp4(int dev, int M, int N, int K, bool sfa_aligned16, int* variant) {
+  const uint32_t sms = static_cast<uint32_t>(g_dev[dev].sms);
+  const uint32_t max_pairs = static_cast<uint32_t>(g_dev[dev].max_fp8fp4_pairs);
+  const bool pairs_ok = max_pairs > 0 && K % 512 == 0 && sfa_aligned16;
+  *variant = ceil_div(M, 128) * ceil_div(N, 256) >= sms ? 1 : 0;
+  if (pairs_ok && ceil_div(M, 256) * ceil_div(N, 256) >= max_pairs) *variant = 2;
+  if (const char* env = getenv("ARC_FP8FP4_KERNEL")) {
+    if (strcmp(env, "pair") == 0) {
+      if (!pairs_ok) {
+        return fail(ARC_ERR_UNSUPPORTED,
+                    "ARC_FP8FP4_KERNEL=pair needs K %% 512 == 0, a 16-byte aligned sfa and a co-resident CTA pair");
+      }
+      *variant = 2;
+    } else if (strcmp(env, "128") == 0) {
+      *variant = 0;
+    } else if (strcmp(env, "256") == 0) {
+      *variant = 1;
+    } else {
+      return fail(ARC_ERR_INVALID_ARGUMENT, "ARC_FP8FP4_KERNEL must be 128, 256 or pair (got '%s')", env);
+    }
+  }
+  return ARC_OK;
+}
+
 }  // namespace
 
 // =================================================================================
@@ -495,6 +545,41 @@ const char* arc_status_string(int status) {
 }
 
 const char* arc_last_error(void) { return g_last_error; }
+
+int arc_kernel_name(int op, int M, int N, int K, char* name, int len) {
+  g_last_error[0] = '\0';
+  if (name == nullptr || len <= 0 || M <= 0 || N <= 0 || K <= 0) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_kernel_name: bad argument");
+  }
+  int dev = 0;
+  if (int st = current_device(&dev)) return st;
+  const char* kernel = nullptr;
+  if (op == ARC_OP_MATMUL_BF16) {
+    bool pairs = false;
+    if (int st = choose_bf16(dev, M, N, &pairs)) return st;
+    kernel = pairs ? "gemm_bf16_pair_kernel" : "gemm_bf16_kernel";
+  } else if (op == ARC_OP_A8W4) {
+    if (K % static_cast<int>(arcb::a8w4::kGroupK) != 0) {
+      return fail(ARC_ERR_UNSUPPORTED, "arc_kernel_name: K must be a multiple of 128");
+    }
+    arc_a8w4_plan_t plan;
+    plan_a8w4(M, N, K, g_dev[dev].sms, g_dev[dev].max_clusters2, g_dev[dev].max_clusters4, &plan);
+    if (M <= static_cast<int>(kDecodeMaxM)) {
+      kernel = plan.token_tile == 16 ? "gemm_a8w4_decode_kernel<16>" : "gemm_a8w4_decode_kernel<32>";
+    } else {
+      kernel = plan.token_tile == 64 ? "gemm_a8w4_kernel<64,1,4>" : "gemm_a8w4_kernel<128,2,3>";
+    }
+  } else if (op == ARC_OP_FP8_FP4) {
+    int variant = 0;
+    if (int st = choose_fp8fp4(dev, M, N, K, true, &variant)) return st;
+    kernel = variant == 2 ? "gemm_fp8fp4_pair_kernel"
+                          : (variant == 1 ? "gemm_fp8fp4_kernel<2>" : "gemm_fp8fp4_kernel<1>");
+  } else {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_kernel_name: unknown op %d", op);
+  }
+  snprintf(name, static_cast<size_t>(len), "%s", kernel);
+  return ARC_OK;
+}
 
 int arc_matmul_bf16(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
                     int ldc, cudaStream_t stream) {
@@ -519,21 +604,9 @@ int arc_matmul_bf16(const void* A, const void* B, void* C, int M, int N, int K, 
   int dev = 0;
   if (int st = current_device(&dev)) return st;
   const uint32_t sms = static_cast<uint32_t>(g_dev[dev].sms);
-  // CTA pairs (256 x 256 tiles, half the shared-memory traffic per MAC) once the pair
-  // tiles fill at least half the SMs; one CTA per 128 x 256 tile below that.
-  // ARC_BF16_CTAS=1|2 forces one (tests and tuning).
   const uint32_t max_pairs = static_cast<uint32_t>(g_dev[dev].max_bf16_pairs);
-  bool pairs = max_pairs > 0 && static_cast<uint32_t>(ceil_div(M, 256) * ceil_div(N, 256)) * 4 >= sms;
-  if (const char* env = getenv("ARC_BF16_CTAS")) {
-    const int v = atoi(env);
-    if (v != 1 && v != 2) {
-      return fail(ARC_ERR_INVALID_ARGUMENT, "ARC_BF16_CTAS must be 1 or 2 (got '%s')", env);
-    }
-    pairs = v == 2;
-    if (pairs && max_pairs == 0) {
-      return fail(ARC_ERR_UNSUPPORTED, "ARC_BF16_CTAS=2: no CTA pair of the bf16 kernel fits on this device");
-    }
-  }
+  bool pairs = false;
+  if (int st = choose_bf16(dev, M, N, &pairs)) return st;
   if (pairs) {
     namespace P2 = arcb::bf16pair;
     P2::Params p;
@@ -751,24 +824,10 @@ int arc_fp8_fp4_gemm(const uint8_t* A, const float* sfa, const uint8_t* Wp, cons
   // SMs; else 128-row tiles (twice the CTAs, e.g. for decode batches).
   // ARC_FP8FP4_KERNEL=128|256|pair forces one (tests and tuning).
   const uint32_t max_pairs = static_cast<uint32_t>(g_dev[dev].max_fp8fp4_pairs);
-  uint32_t rows = ceil_div(M, F::kBT) * ceil_div(N, 256) >= sms ? 256u : 128u;
-  const bool pairs_ok = max_pairs > 0 && K % 512 == 0 && aligned16(sfa);
-  bool pairs = pairs_ok && ceil_div(M, 256) * ceil_div(N, 256) >= max_pairs;
-  if (const char* env = getenv("ARC_FP8FP4_KERNEL")) {
-    if (strcmp(env, "pair") == 0) {
-      if (!pairs_ok) {
-        return fail(ARC_ERR_UNSUPPORTED,
-                    "ARC_FP8FP4_KERNEL=pair needs K %% 512 == 0, a 16-byte aligned sfa and a co-resident CTA pair");
-      }
-      pairs = true;
-    } else if (strcmp(env, "128") == 0 || strcmp(env, "256") == 0) {
-      rows = static_cast<uint32_t>(atoi(env));
-      pairs = false;
-    } else {
-      return fail(ARC_ERR_INVALID_ARGUMENT, "ARC_FP8FP4_KERNEL must be 128, 256 or pair (got '%s')", env);
-    }
-  }
-  if (pairs) {
+  int variant = 0;
+  if (int st = choose_fp8fp4(dev, M, N, K, aligned16(sfa), &variant)) return st;
+  const uint32_t rows = variant == 1 ? 256u : 128u;
+  if (variant == 2) {
     namespace FP = arcb::fp8fp4pair;
     FP::Params q;
     if (int st = encode_tokens_3d(&q.tm_tok, A, M, K, 128, 1)) return st;

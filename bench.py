@@ -299,6 +299,14 @@ def build_inputs(wl, rank, device, n_sets):
     return sets
 
 
+def kernel_launched(wl, M, N, K):
+    """The kernel the library launches for this workload's shape (as ncu names it)."""
+    import arc
+    from arc import _lib
+    op = {"a8w4": _lib.OP_A8W4, "fp8fp4": _lib.OP_FP8_FP4}.get(wl["kind"], _lib.OP_MATMUL_BF16)
+    return arc.kernel_name(op, M, N, K)
+
+
 def run_ours(args, wl, world, rank, local):
     import torch
 
@@ -462,8 +470,7 @@ def run_ours(args, wl, world, rank, local):
                      "frac": achieved / peak, "traffic": traffic,
                      "peak_source": peak_note,
                      "algorithmic_per_launch": step_bytes if bound == "hbm" else ops,
-                     "kernel": {"a8w4": "gemm_a8w4_kernel", "fp8fp4": "gemm_fp8fp4_kernel"}.get(
-                         wl["kind"], "gemm_bf16_kernel")},
+                     "kernel": kernel_launched(wl, M, N, K)},
         "e2e": {"value": world * ops / (e2e_ms * 1e-3) / 1e12,
                 "unit": "TOPS" if wl["kind"] == "a8w4" else "TFLOP/s",
                 "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],

@@ -113,7 +113,9 @@ int arc_a8w4_describe_plan(int M, int N, int K, int num_sms, arc_a8w4_plan_t *pl
  *                    k in the low nibble (arc/testing/quant.py:51-84)
  *   sfw  [N][K/32]   fp32 powers of two
  *   C    [M][N]      bf16 (uint16 storage)
- * Requirements: K % 128 == 0; N % 8 == 0; M, N >= 1; A, Wp, C, sfw 16-byte aligned.
+ * Requirements: K % 128 == 0; N % 8 == 0; M, N >= 1; A, C, sfw 16-byte aligned, Wp
+ * 32-byte aligned, sfa 4-byte aligned. Large problems with K % 512 == 0 and a 16-byte
+ * aligned sfa run on CTA pairs.
  */
 int arc_fp8_fp4_gemm(const uint8_t *A, const float *sfa, const uint8_t *Wp, const float *sfw,
                      uint16_t *C, int M, int N, int K, cudaStream_t stream);
@@ -143,6 +145,19 @@ int arc_quantize_int8(const void *x, int8_t *q, float *sa, int M, int K, int ldx
  * arc/include/mm.cuh:201-211). Returns ARC_ERR_UNSUPPORTED in regular builds.
  */
 int arc_probe_attach(void *buffer, size_t bytes);
+
+/*
+ * Name of the kernel the library launches for an operation of this shape on the
+ * current device (op: ARC_OP_MATMUL_BF16, ARC_OP_A8W4 or ARC_OP_FP8_FP4; the FP8 x FP4
+ * answer assumes a 16-byte aligned sfa), e.g. "gemm_bf16_pair_kernel", written into
+ * name[0..len). The shape is not checked beyond what the choice needs; the
+ * ARC_BF16_CTAS / ARC_FP8FP4_KERNEL overrides apply. The reference has one kernel per
+ * operation, so it has no counterpart; this serves profiling (matching ncu launch lists).
+ */
+#define ARC_OP_MATMUL_BF16 0
+#define ARC_OP_A8W4 1
+#define ARC_OP_FP8_FP4 2
+int arc_kernel_name(int op, int M, int N, int K, char *name, int len);
 
 /*
  * Device status word of `device`: a bit mask of the pipeline waits that timed out

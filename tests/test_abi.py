@@ -64,6 +64,15 @@ def test_invalid_arguments_are_rejected_before_any_cuda_call(native_lib):
     assert L.arc_quantize_int8(p, nul, p, 4, 64, 64, 64, nul) == _lib.ARC_ERR_INVALID_ARGUMENT
     assert L.arc_quantize_int8(p, p, p, 4, 64, 32, 64, nul) == _lib.ARC_ERR_INVALID_ARGUMENT
     assert L.arc_quantize_int8(p + 1, p, p, 4, 64, 64, 64, nul) == _lib.ARC_ERR_UNSUPPORTED
+    # FP8 x FP4: K not a multiple of 128, misaligned packed weights (32 bytes needed)
+    assert L.arc_fp8_fp4_gemm(p, p, p, p, p, 16, 64, 200, nul) == _lib.ARC_ERR_UNSUPPORTED
+    a32 = (p + 31) // 32 * 32  # 32-byte aligned inside the buffer
+    assert L.arc_fp8_fp4_gemm(a32, a32, a32 + 16, a32, a32, 16, 64, 256, nul) == \
+        _lib.ARC_ERR_UNSUPPORTED
+    # kernel-name query: no buffer / non-positive sizes
+    assert L.arc_kernel_name(0, 8, 8, 8, nul, 16) == _lib.ARC_ERR_INVALID_ARGUMENT
+    assert L.arc_kernel_name(0, 0, 8, 8, ctypes.cast(buf, ctypes.c_char_p), 16) == \
+        _lib.ARC_ERR_INVALID_ARGUMENT
 
 
 @pytest.mark.parametrize("m,n,k,expect", [
