@@ -474,12 +474,12 @@ cudaError_t launch_ex(Kern kernel, const P& p, uint32_t grid, uint32_t threads, 
 }
 
 // bf16 kernel choice. CTA pairs (256 x 256 tiles, half the shared-memory traffic per
-// MAC) once the pair tiles fill at least half the SMs; one CTA per 128 x 256 tile below
-// that. ARC_BF16_CTAS=1|2 forces one (tests and tuning).
+// MAC) once the pair tiles give every co-resident pair one; one CTA per 128 x 256 tile
+// below that (e.g. 2048^3: 64 pair tiles would leave 20 SMs idle, 128 one-CTA tiles
+// fill as many). ARC_BF16_CTAS=1|2 forces one (tests and tuning).
 int choose_bf16(int dev, int M, int N, bool* pairs) {
-  const uint32_t sms = static_cast<uint32_t>(g_dev[dev].sms);
   const uint32_t max_pairs = static_cast<uint32_t>(g_dev[dev].max_bf16_pairs);
-  *pairs = max_pairs > 0 && static_cast<uint32_t>(ceil_div(M, 256) * ceil_div(N, 256)) * 4 >= sms;
+  *pairs = max_pairs > 0 && static_cast<uint32_t>(ceil_div(M, 256) * ceil_div(N, 256)) >= max_pairs;
   if (const char* env = getenv("ARC_BF16_CTAS")) {
     const int v = atoi(env);
     if (v != 1 && v != 2) {
