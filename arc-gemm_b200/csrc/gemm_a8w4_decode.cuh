@@ -200,6 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // has completed and its writes are visible.
   pdl_wait();
   if (threadIdx.x == 0) probe_mark(2);  // previous grid complete
+  bool cl_arrived = false;  // this thread's arrival on the end-of-kernel cluster barrier
   const uint32_t tmem_base = s.tmem_base;
 
   if (warp == 0) {
@@ -212,8 +213,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (uint32_t idx = 0; ok && get_item(p, idx, it); ++idx) {
         for (uint32_t g = it.g0; g < it.g1; g += p.gps, ++q) {
           const uint32_t st = q % p.stages;
-          if (!mbar_wait(&s.load_empty[st], ((q / p.stages) & 1u) ^ 1u, abort,
-                         kStatusTimeoutProducer)) {
+          // The first fill of each stage needs no wait (a wait on a fresh barrier still
+          // costs ~240 cycles of this thread's time before the first load goes out).
+          if (q >= p.stages && !mbar_wait(&s.load_empty[st], ((q / p.stages) & 1u) ^ 1u, abort,
+                                          kStatusTimeoutProducer)) {
             ok = false;
             break;
           }
@@ -484,6 +487,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const bool got = warp_wait(&s.recv_full, 0, abort, kStatusTimeoutEpilogue);
         if (et == 0) probe_mark(5);  // peer partials landed
+        // Nothing targets this CTA's shared memory any more: announce it now and wait at
+        // the end, so the cluster barrier overlaps the reduction and the store.
+        if (!cl_arrived) {
+          __syncwarp();
+          cluster_arrive();
+          cl_arrived = true;
+        }
         if (got) {
           const float* own = send + rank * rows_per * BT;
           for (uint32_t e = et; e < rows_per * BT; e += 128) {
@@ -511,9 +521,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 64) probe_mark(15);  // TMEM allocator warp reached the end
   if (p.S > 1) {
     // No CTA leaves while a bulk copy may still target its shared memory: owners
-    // pass this only after their recv_full wait (or its timeout).
+    // arrive only after their recv_full wait (or its timeout), every other thread
+    // when its role is done.
     __syncwarp();
-    cluster_sync_all();
+    if (!cl_arrived) cluster_arrive();
+    cluster_wait();
     if (threadIdx.x == 0) probe_mark(14);  // end-of-kernel cluster barrier passed
   }
 

@@ -479,6 +479,14 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
                    : "memory");
 }
+// The two halves of cluster_sync_all, for a thread that can announce early that it is
+// done and wait later (every thread of the cluster arrives once, then waits once).
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 
 // Address of the same shared-memory object in CTA `rank` of this cluster.
 __device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
