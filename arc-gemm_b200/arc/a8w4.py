@@ -18,6 +18,7 @@ Everything runs in `arc_a8w4_gemm` (include/arc_b200.h) on the caller's stream.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Sequence
 
 import torch
@@ -167,7 +168,32 @@ def fp8_fp4_gemm_nt(a: TensorPair, b: TensorPair, out: torch.Tensor,
     _expect(sfw, "b[1]", torch.float32, (n, k // 32), dev)
     _expect(out, "out", torch.bfloat16, (m, n), dev)
     with torch.cuda.device(dev):
-        check(lib().arc_fp8_fp4_gemm(x.data_ptr(), sfa.data_ptr(), wp.data_ptr(), sfw.data_ptr(),
-                                     out.data_ptr(), m, n, k, _stream_ptr(dev)),
+        ws = _fp8_fp4_workspace(dev, m, n, k)
+        check(lib().arc_fp8_fp4_gemm_ws(x.data_ptr(), sfa.data_ptr(), wp.data_ptr(), sfw.data_ptr(),
+                                        out.data_ptr(), m, n, k,
+                                        ws.data_ptr() if ws is not None else None,
+                                        ws.numel() if ws is not None else 0, _stream_ptr(dev)),
               "arc.fp8_fp4_gemm_nt")
     return out
+
+
+# One zeroed workspace per (device, stream), grown on demand: the K split of decode-sized
+# problems keeps fp32 partials and per-tile counters in it, and every call leaves the
+# counters at zero again. Keyed by stream so that calls that may run concurrently (on
+# different streams) never share one.
+_WORKSPACES: dict = {}
+
+
+def _fp8_fp4_workspace(dev: torch.device, m: int, n: int, k: int):
+    need = ctypes.c_size_t(0)
+    check(lib().arc_fp8_fp4_workspace_bytes(m, n, k, ctypes.byref(need)), "arc_fp8_fp4_workspace_bytes")
+    if need.value == 0:
+        return None
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < need.value:
+        ws = torch.zeros(need.value + 256, dtype=torch.uint8, device=dev)
+        off = (-ws.data_ptr()) % 256  # 256-byte aligned view
+        ws = ws[off:off + need.value]
+        _WORKSPACES[key] = ws
+    return ws

@@ -523,6 +523,49 @@ int choose_fp8fp4(int dev, int M, int N, int K, bool sfa_aligned16, int* variant
   return ARC_OK;
 }
 
+// K split of the one-CTA FP8 x FP4 kernel for problems with fewer 128 x 128 tiles than
+// SMs (decode batches): S CTAs per tile (2, 4 or 8, all resident in one wave), each
+// taking gs K groups (a multiple of 2, the groups per stage). Workspace: one uint32
+// counter per tile in a fixed 4 KB head (a split problem has fewer tiles than SMs), then
+// S fp32 partials of [M][N]. The head never holds partials, so one workspace serves
+// problems of any shape in turn: the kernel leaves every counter at zero.
+constexpr size_t kSplitCounterBytes = 4096;
+struct SplitPlan {
+  uint32_t S, gs;
+  size_t partial_offset, bytes;
+};
+SplitPlan fp8fp4_split_plan(int dev, int M, int N, int K) {
+  SplitPlan sp{1, static_cast<uint32_t>(K / 128), 0, 0};
+  const uint32_t sms = static_cast<uint32_t>(g_dev[dev].sms);
+  const uint32_t G = static_cast<uint32_t>(K / 128);
+  const uint32_t tiles = static_cast<uint32_t>(ceil_div(M, 128) * ceil_div(N, 128));
+  uint32_t S = 1;
+  for (uint32_t c : {8u, 4u, 2u}) {
+    if (tiles * c <= sms && G >= 2 * c) {
+      S = c;
+      break;
+    }
+  }
+  if (const char* env = getenv("ARC_FP8FP4_SPLIT")) {  // tests and tuning
+    const int v = atoi(env);
+    if (v >= 1 && v <= 16 && static_cast<uint32_t>(v) * 2 <= G) S = static_cast<uint32_t>(v);
+  }
+  if (S <= 1) return sp;
+  uint32_t gs = (G + S - 1) / S;
+  gs += gs & 1u;
+  S = (G + gs - 1) / gs;  // no empty splits
+  if (S <= 1) return sp;
+  sp.S = S;
+  sp.gs = gs;
+  if (size_t(tiles) * sizeof(uint32_t) > kSplitCounterBytes) return SplitPlan{1, G, 0, 0};
+  sp.partial_offset = kSplitCounterBytes;
+  sp.bytes = kSplitCounterBytes + size_t(S) * M * N * sizeof(float);
+  return sp;
+}
+
+int fp8fp4_gemm(const uint8_t* A, const float* sfa, const uint8_t* Wp, const float* sfw, uint16_t* C,
+                int M, int N, int K, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 }  // namespace
 
 // =================================================================================
@@ -798,6 +841,38 @@ int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uin
 int arc_fp8_fp4_gemm(const uint8_t* A, const float* sfa, const uint8_t* Wp, const float* sfw,
                      uint16_t* C, int M, int N, int K, cudaStream_t stream) {
   g_last_error[0] = '\0';
+  return fp8fp4_gemm(A, sfa, Wp, sfw, C, M, N, K, nullptr, 0, stream);
+}
+
+int arc_fp8_fp4_workspace_bytes(int M, int N, int K, size_t* bytes) {
+  g_last_error[0] = '\0';
+  if (bytes == nullptr || M <= 0 || N <= 0 || K <= 0 || K % 128 != 0) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_fp8_fp4_workspace_bytes: bad argument");
+  }
+  int dev = 0;
+  if (int st = current_device(&dev)) return st;
+  int variant = 0;
+  if (int st = choose_fp8fp4(dev, M, N, K, true, &variant)) return st;
+  *bytes = variant == 0 ? fp8fp4_split_plan(dev, M, N, K).bytes : 0;
+  return ARC_OK;
+}
+
+int arc_fp8_fp4_gemm_ws(const uint8_t* A, const float* sfa, const uint8_t* Wp, const float* sfw,
+                        uint16_t* C, int M, int N, int K, void* workspace, size_t workspace_bytes,
+                        cudaStream_t stream) {
+  g_last_error[0] = '\0';
+  if (workspace != nullptr && (reinterpret_cast<uintptr_t>(workspace) & 255u)) {
+    return fail(ARC_ERR_UNSUPPORTED, "arc_fp8_fp4_gemm_ws: the workspace must be 256-byte aligned");
+  }
+  return fp8fp4_gemm(A, sfa, Wp, sfw, C, M, N, K, workspace, workspace_bytes, stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+int fp8fp4_gemm(const uint8_t* A, const float* sfa, const uint8_t* Wp, const float* sfw, uint16_t* C,
+                int M, int N, int K, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (A == nullptr || sfa == nullptr || Wp == nullptr || sfw == nullptr || C == nullptr) {
     return fail(ARC_ERR_INVALID_ARGUMENT, "arc_fp8_fp4_gemm: null pointer");
   }
@@ -870,13 +945,31 @@ int arc_fp8_fp4_gemm(const uint8_t* A, const float* sfa, const uint8_t* Wp, cons
   p.tiles_m = ceil_div(M, F::kBT);
   p.tiles_n = ceil_div(N, rows);
   p.num_tiles = p.tiles_m * p.tiles_n;
-  const uint32_t grid = p.num_tiles < sms ? p.num_tiles : sms;
+  p.S = 1;
+  p.gs = p.G;
+  p.ws = nullptr;
+  p.counters = nullptr;
+  if (variant == 0 && workspace != nullptr) {
+    const SplitPlan sp = fp8fp4_split_plan(dev, M, N, K);
+    if (sp.S > 1 && workspace_bytes >= sp.bytes) {
+      p.S = sp.S;
+      p.gs = sp.gs;
+      p.counters = static_cast<uint32_t*>(workspace);
+      p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + sp.partial_offset);
+    }
+  }
+  const uint32_t items = p.num_tiles * p.S;
+  const uint32_t grid = items < sms ? items : sms;
   const cudaError_t e =
       rows == 256 ? launch_ex(F::gemm_fp8fp4_kernel<2>, p, grid, F::kThreads, sizeof(F::Smem<2>) + 1024, 1, stream)
                   : launch_ex(F::gemm_fp8fp4_kernel<1>, p, grid, F::kThreads, sizeof(F::Smem<1>) + 1024, 1, stream);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_fp8fp4_kernel launch");
   return ARC_OK;
 }
+
+}  // namespace
+
+extern "C" {
 
 int arc_quantize_int8(const void* x, int8_t* q, float* sa, int M, int K, int ldx, int ldq,
                       cudaStream_t stream) {

@@ -97,6 +97,14 @@ struct Params {
   uint32_t M, N, K, G;
   uint32_t ldsfa, ldsfw, ldc;
   uint32_t tiles_m, tiles_n, num_tiles;
+  // K split (S > 1, for problems with fewer tiles than SMs): the S CTAs of a tile each
+  // take gs consecutive K groups (a multiple of the groups per stage), write their fp32
+  // partial to ws[split][m][n] and count themselves in counters[tile]; the last one
+  // sums the S partials in split order (deterministic), stores the bf16 tile and
+  // resets its counter to zero for the next call.
+  uint32_t S, gs;
+  float* ws;
+  uint32_t* counters;
 };
 
 template <uint32_t H>
@@ -113,6 +121,7 @@ struct alignas(1024) Smem {
   uint64_t tmem_empty[C::kAccBufs];
   uint32_t tmem_base;
   uint32_t abort;
+  uint32_t last;  // K split: this CTA was the last of its tile
 };
 static_assert(sizeof(Smem<1>) + 1024 <= 232448, "shared memory (with alignment slack) fits in 227 KB");
 static_assert(sizeof(Smem<2>) + 1024 <= 232448, "shared memory (with alignment slack) fits in 227 KB");
@@ -134,11 +143,14 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 // Work decomposition: bands of 4 token tiles sweep all weight tiles, so a wave of CTAs
 // shares a few token tiles and each weight tile is read by up to 4 neighbouring CTAs.
+// With a K split, work item t is split t % S of tile t / S (the splits of a tile are
+// neighbours in launch order, so they run at the same time).
 template <uint32_t H>
 __device__ __forceinline__ bool next_tile(const Params& p, uint32_t& cursor, Work& w) {
-  const uint32_t t = blockIdx.x + cursor * gridDim.x;
-  if (t >= p.num_tiles) return false;
+  const uint32_t item = blockIdx.x + cursor * gridDim.x;
+  if (item >= p.num_tiles * p.S) return false;
   ++cursor;
+  const uint32_t t = item / p.S, split = item - t * p.S;
   constexpr uint32_t kBand = 4;
   const uint32_t band = t / (kBand * p.tiles_n);
   const uint32_t rem = t - band * kBand * p.tiles_n;
@@ -146,8 +158,8 @@ __device__ __forceinline__ bool next_tile(const Params& p, uint32_t& cursor, Wor
   const uint32_t m_cnt = min(kBand, p.tiles_m - m_first);
   w.m0 = (m_first + rem % m_cnt) * kBT;
   w.n0 = (rem / m_cnt) * Cfg<H>::kRows;
-  w.g_begin = 0;
-  w.g_end = p.G;
+  w.g_begin = split * p.gs;
+  w.g_end = min(p.G, w.g_begin + p.gs);
   return true;
 }
 
@@ -415,8 +427,67 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8fp4_kernel(const __grid_c
         break;
       }
       tc_fence_after_sync();
-      uint32_t packed[kCols / 2];
       const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * C::kAccCols + h * kBT + c0;
+      const uint32_t n = w.n0 + nl;
+      const uint32_t m_first = w.m0 + c0;
+      if (p.S > 1) {
+        // K split: this CTA's fp32 partial goes to ws[split] (only rows m < M), then
+        // the last CTA of the tile reduces.
+        const uint32_t split = w.g_begin / p.gs;
+        const bool mine = n < p.N && m_first < p.M;
+        const uint32_t m_cnt = mine ? min(kCols, p.M - m_first) : 0u;
+        float* wp_ = p.ws + (size_t(split) * p.M + m_first) * p.N + n;
+#pragma unroll
+        for (uint32_t cc = 0; cc < kCols; cc += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + cc, r);
+          tmem_ld_wait();
+          if (cc < m_cnt) {
+#pragma unroll
+            for (uint32_t j = 0; j < 32; ++j) {
+              if (cc + j < m_cnt) wp_[size_t(cc + j) * p.N] = __uint_as_float(r[j]);
+            }
+          }
+        }
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.tmem_empty[acc]);
+        __threadfence();  // the partial is visible device-wide before this CTA is counted
+        named_barrier_sync(2, 32 * kEpiWarps);
+        const uint32_t tile = (blockIdx.x + (cursor - 1u) * gridDim.x) / p.S;
+        if (threadIdx.x == 256) s.last = atomicAdd(p.counters + tile, 1u) == p.S - 1u ? 1u : 0u;
+        named_barrier_sync(2, 32 * kEpiWarps);
+        if (*reinterpret_cast<volatile uint32_t*>(&s.last) != 0u) {
+          __threadfence();
+          // 32 rows at a time, split-major: each split's 32 loads are independent, so
+          // the reduction costs ~S L2 round trips, not S x rows.
+          for (uint32_t cc = 0; cc < m_cnt; cc += 32) {
+            float sum[32];
+#pragma unroll
+            for (uint32_t j = 0; j < 32; ++j) sum[j] = 0.f;
+            for (uint32_t r = 0; r < p.S; ++r) {
+              const float* src = p.ws + (size_t(r) * p.M + m_first + cc) * p.N + n;
+              // Unpredicated loads (rows past m_cnt re-read the last valid row) so that
+              // all 32 are in flight together.
+              float v[32];
+#pragma unroll
+              for (uint32_t j = 0; j < 32; ++j) v[j] = __ldcg(src + size_t(min(cc + j, m_cnt - 1u) - cc) * p.N);
+#pragma unroll
+              for (uint32_t j = 0; j < 32; ++j) sum[j] += v[j];
+            }
+#pragma unroll
+            for (uint32_t j = 0; j < 32; ++j) {
+              if (cc + j < m_cnt) {
+                p.out[size_t(m_first + cc + j) * p.ldc + n] = __bfloat16_as_ushort(__float2bfloat16_rn(sum[j]));
+              }
+            }
+          }
+          if (threadIdx.x == 256) p.counters[tile] = 0u;  // ready for the next call
+        }
+        ++ti;
+        continue;
+      }
+      uint32_t packed[kCols / 2];
       // 32 columns at a time, so the raw and the packed values fit in registers.
 #pragma unroll
       for (uint32_t cc = 0; cc < kCols; cc += 32) {
@@ -430,8 +501,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8fp4_kernel(const __grid_c
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.tmem_empty[acc]);
       if (threadIdx.x == 256 && ti < 4u) probe_mark(32 + ti);
-      const uint32_t n = w.n0 + nl;
-      const uint32_t m_first = w.m0 + c0;
       if (n < p.N && m_first < p.M) {
         const uint32_t m_cnt = min(kCols, p.M - m_first);
         uint16_t* o = p.out + size_t(m_first) * p.ldc + n;

@@ -121,6 +121,27 @@ int arc_fp8_fp4_gemm(const uint8_t *A, const float *sfa, const uint8_t *Wp, cons
                      uint16_t *C, int M, int N, int K, cudaStream_t stream);
 
 /*
+ * The same GEMM with a caller-owned workspace, which lets problems with fewer 128 x 128
+ * output tiles than SMs (decode batches) split K over several CTAs per tile: each writes
+ * an fp32 partial into the workspace and the last one of a tile sums them in a fixed
+ * order (results do not depend on timing) and stores the tile. Same role and call shape
+ * as arc_fp8_fp4_gemm (tests/a8w4.py:48); the workspace has no counterpart there.
+ *   workspace   256-byte aligned device memory of at least
+ *               arc_fp8_fp4_workspace_bytes(M, N, K) bytes, all ZERO before its first use;
+ *               every call leaves it ready for the next (its tile counters back at zero)
+ *               unless a kernel wait timed out (arc_device_status), after which it must be
+ *               zeroed again. Calls that share a workspace must not run concurrently.
+ *   A NULL or too small workspace runs the GEMM without the K split.
+ */
+int arc_fp8_fp4_gemm_ws(const uint8_t *A, const float *sfa, const uint8_t *Wp, const float *sfw,
+                        uint16_t *C, int M, int N, int K, void *workspace, size_t workspace_bytes,
+                        cudaStream_t stream);
+
+/* Workspace bytes arc_fp8_fp4_gemm_ws uses for this shape on the current device (0: no
+ * K split for it). */
+int arc_fp8_fp4_workspace_bytes(int M, int N, int K, size_t *bytes);
+
+/*
  * Per-token int8 quantisation of bf16 activations, the producer of the A8W4 GEMM's
  * activation operand:
  *   amax[m] = max(max_k |x[m,k]|, 1e-4),  sa[m] = amax[m] / 127  (fp32),

@@ -65,3 +65,30 @@ def test_fp8_fp4_gemm_rejects_other_recipes(cuda_device):
     with pytest.raises(ValueError):
         arc.fp8_fp4_gemm_nt((x.to(cuda_device), sfa.to(cuda_device)),
                             (wp.to(cuda_device), sfw.to(cuda_device)), out, recipe_b=(1, 128))
+
+
+@pytest.mark.parametrize("split", [2, 3, 4])
+@pytest.mark.parametrize("m,n,k", [(16, 4096, 4096), (1, 264, 1152), (33, 520, 2048)])
+def test_fp8_fp4_gemm_k_split(cuda_device, monkeypatch, m, n, k, split):
+    """Decode-sized problems split K over several CTAs per tile (the workspace path of
+    arc.fp8_fp4_gemm_nt): forced split counts, including a ragged last split and one
+    of a single group (K = 1152 has 9 groups). The result equals the unsplit kernel's
+    within the same tolerance, and two calls in a row give identical bits (the partials
+    are summed in a fixed order, and the tile counters are left at zero)."""
+    monkeypatch.setenv("ARC_FP8FP4_KERNEL", "128")
+    monkeypatch.setenv("ARC_FP8FP4_SPLIT", str(split))
+    a_ref, b_ref, (x, sfa), (wp, sfw) = _data(m, n, k, seed=7 * m + n + k)
+    dev = cuda_device
+    xs, sas, wps, sfws = x.to(dev), sfa.to(dev), wp.to(dev), sfw.to(dev)
+    outs = []
+    for _ in range(2):
+        out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=dev)
+        arc.fp8_fp4_gemm_nt((xs, sas), (wps, sfws), out, recipe_a=(1, 128), recipe_b=(1, 32))
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert arc.device_status(0) == 0, "kernel reported a wait timeout"
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+    got = outs[0].float().cpu().numpy()
+    ref = oracle.fp8fp4_out(x.view(torch.uint8).numpy(), sfa.numpy(), wp.numpy(), sfw.numpy())
+    ok, msg = oracle.check_bf16_close(got, ref, max_ulp=2.0, atol=oracle.tensor_core_atol(k, ref))
+    assert ok, f"{m}x{n}x{k} split={split}: {msg}"
