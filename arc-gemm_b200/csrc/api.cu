@@ -869,6 +869,69 @@ int arc_fp8_fp4_gemm_ws(const uint8_t* A, const float* sfa, const uint8_t* Wp, c
 
 }  // extern "C"
 
+// ---------------------------------------------------------------------------------
+// Allocation-free FP8 x FP4 GEMM. Some callers cannot hand this library a workspace:
+// plugins whose host framework budgets every byte of device memory itself and offers
+// the operator nothing beyond its input and output tensors, and hosts that must not call
+// cudaMalloc on the request path (it can synchronise the device and its latency is not
+// bounded). For them the K split's scratch lives in a fixed device array built into the
+// library, 4 MiB on every GPU that loads it, held until the process exits.
+// ---------------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
+
+struct NoAllocScratch {
+  std::once_flag once;
+  cudaError_t err = cudaSuccess;
+  void* ptr = nullptr;  // device address of the array on this device
+};
+NoAllocScratch g_noalloc[kMaxDevices];
+
+}  // namespace
+
+// In host code this name is a host-side stand-in, not a device address; the device
+// address comes from cudaGetSymbolAddress, once per device, with that device current.
+static __device__ __align__(256) unsigned char g_fp8fp4_noalloc_scratch[kNoAllocScratchBytes];
+
+extern "C" int arc_fp8_fp4_gemm_noalloc(const uint8_t* A, const float* sfa, const uint8_t* Wp,
+                                        const float* sfw, uint16_t* C, int M, int N, int K,
+                                        cudaStream_t stream) {
+  g_last_error[0] = '\0';
+  if (M <= 0 || N <= 0 || K <= 0 || K % 128 != 0) {
+    return fail(ARC_ERR_INVALID_ARGUMENT,
+                "arc_fp8_fp4_gemm_noalloc: need positive sizes and K %% 128 == 0 (M=%d N=%d K=%d)", M, N,
+                K);
+  }
+  int dev = 0;
+  if (int st = current_device(&dev)) return st;
+  int variant = 0;
+  if (int st = choose_fp8fp4(dev, M, N, K, aligned16(sfa), &variant)) return st;
+  const size_t need = variant == 0 ? fp8fp4_split_plan(dev, M, N, K).bytes : 0;
+  if (need > kNoAllocScratchBytes) {
+    return fail(ARC_ERR_UNSUPPORTED,
+                "arc_fp8_fp4_gemm_noalloc: M=%d N=%d K=%d needs %zu bytes of scratch for its K split; the "
+                "built-in scratch holds %zu (use arc_fp8_fp4_gemm_ws with a workspace of your own)",
+                M, N, K, need, kNoAllocScratchBytes);
+  }
+  if (need == 0) {  // no K split for this shape: no scratch either
+    return fp8fp4_gemm(A, sfa, Wp, sfw, C, M, N, K, nullptr, 0, stream);
+  }
+  NoAllocScratch& sc = g_noalloc[dev];
+  std::call_once(sc.once, [&sc] {
+    sc.err = cudaGetSymbolAddress(&sc.ptr, g_fp8fp4_noalloc_scratch);
+    if (sc.err != cudaSuccess) cudaGetLastError();
+  });
+  if (sc.err != cudaSuccess || sc.ptr == nullptr) {
+    return cuda_fail(sc.err != cudaSuccess ? sc.err : cudaErrorInvalidSymbol,
+                     "arc_fp8_fp4_gemm_noalloc: cudaGetSymbolAddress of the built-in scratch");
+  }
+  // The array keeps the previous call's contents: the tile counters must start at zero.
+  const cudaError_t e = cudaMemsetAsync(sc.ptr, 0, kSplitCounterBytes, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "arc_fp8_fp4_gemm_noalloc: clearing the scratch counters");
+  return fp8fp4_gemm(A, sfa, Wp, sfw, C, M, N, K, sc.ptr, kNoAllocScratchBytes, stream);
+}
+
 namespace {
 
 int fp8fp4_gemm(const uint8_t* A, const float* sfa, const uint8_t* Wp, const float* sfw, uint16_t* C,
