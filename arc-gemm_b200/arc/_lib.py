@@ -60,6 +60,10 @@ SIGNATURES = {
     "arc_fp8_fp4_gemm_ws": ([_P, _P, _P, _P, _P, _I, _I, _I, _P, ctypes.c_size_t, _P], _I),
     "arc_fp8_fp4_workspace_bytes": ([_I, _I, _I, ctypes.POINTER(ctypes.c_size_t)], _I),
     "arc_fp8_fp4_gemm_noalloc": ([_P, _P, _P, _P, _P, _I, _I, _I, _P], _I),
+    "arc_a8w4_gemm_gather": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
+    "arc_peer_barrier": ([_P, _I, _I, ctypes.c_uint32, _P], _I),
+    "arc_a8w4_prepack_weights": ([_P, _P, _I, _I, _P], _I),
+    "arc_a8w4_gemm_prepacked": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _P], _I),
 }
 
 # Operation codes of arc_kernel_name (include/arc_b200.h).

@@ -49,11 +49,14 @@ def _expect(t: torch.Tensor, name: str, dtype: torch.dtype, shape: tuple, device
 
 
 def a8w4_matmul(a: TensorPair, b: TensorPair, out: torch.Tensor | None = None, *,
-                group: int = GROUP_K, partials: torch.Tensor | None = None) -> torch.Tensor:
+                group: int = GROUP_K, partials: torch.Tensor | None = None,
+                prepacked: bool = False) -> torch.Tensor:
     """out = A8W4 GEMM of (x, sa) and (wp, sb). See the module docstring.
 
     `partials`, if given, is an int32 [M, N, K/128] tensor that receives every exact
     group partial P[m, n, g] (a slow debugging mode).
+    `prepacked=True` says wp is in the pre-packed layout of `prepack_weights` (same
+    shape; results identical to the original packing).
     """
     x, sa = a
     wp, sb = b
@@ -75,6 +78,14 @@ def a8w4_matmul(a: TensorPair, b: TensorPair, out: torch.Tensor | None = None, *
     else:
         _expect(out, "out", torch.bfloat16, (m, n), dev)
     pptr = None
+    if prepacked:
+        if partials is not None:
+            raise ValueError("partials are not available with prepacked weights")
+        with torch.cuda.device(dev):
+            check(lib().arc_a8w4_gemm_prepacked(x.data_ptr(), sa.data_ptr(), wp.data_ptr(), sb.data_ptr(),
+                                                out.data_ptr(), m, n, k, group, _stream_ptr(dev)),
+                  "arc.a8w4_matmul")
+        return out
     if partials is not None:
         _expect(partials, "partials", torch.int32, (m, n, k // group), dev)
         pptr = partials.data_ptr()
@@ -82,6 +93,26 @@ def a8w4_matmul(a: TensorPair, b: TensorPair, out: torch.Tensor | None = None, *
         check(lib().arc_a8w4_gemm(x.data_ptr(), sa.data_ptr(), wp.data_ptr(), sb.data_ptr(),
                                   out.data_ptr(), m, n, k, group, _stream_ptr(dev), pptr),
               "arc.a8w4_matmul")
+    return out
+
+
+def prepack_weights(wp: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Packed int4 weights [N, K/2] (the reference's packing, even k in the low nibble)
+    -> the pre-packed layout, on the GPU: inside every 16-byte piece (32 codes of a row),
+    byte j holds code j in its low nibble and code j+16 in its high nibble. `out` may be
+    `wp` itself (in place). Use the result with `a8w4_matmul(..., prepacked=True)`.
+    """
+    if not isinstance(wp, torch.Tensor) or wp.dim() != 2:
+        raise ValueError("wp must be a 2-D uint8 tensor [N, K/2]")
+    n, k2 = wp.shape
+    _expect(wp, "wp", torch.uint8, (n, k2), None)
+    if out is None:
+        out = torch.empty_like(wp)
+    else:
+        _expect(out, "out", torch.uint8, (n, k2), wp.device)
+    with torch.cuda.device(wp.device):
+        check(lib().arc_a8w4_prepack_weights(wp.data_ptr(), out.data_ptr(), n, 2 * k2, _stream_ptr(wp.device)),
+              "arc.prepack_weights")
     return out
 
 

@@ -25,8 +25,8 @@ PROBE_LIB_PATH = PKG_DIR / "libarcb200_probe.so"
 STAMP = ROOT / "_build" / "libarcb200.hash"
 
 SOURCES = ["api.cu"]
-HEADERS = ["sm100.cuh", "gemm_bf16.cuh", "gemm_bf16_pair.cuh", "gemm_a8w4.cuh", "gemm_a8w4_decode.cuh", "quantize.cuh",
-           "gemm_fp8fp4.cuh", "gemm_fp8fp4_pair.cuh"]
+HEADERS = ["sm100.cuh", "peer_barrier.cuh", "gemm_bf16.cuh", "gemm_bf16_pair.cuh", "gemm_a8w4.cuh", "gemm_a8w4_decode.cuh", "quantize.cuh",
+           "gemm_fp8fp4.cuh", "gemm_fp8fp4_pair.cuh", "prepack.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -4,9 +4,11 @@ The reference has no multi-GPU code. The weight matrix shards naturally along N:
 columns and their scales are independent, so rank r of g owns
 W[r*N/g:(r+1)*N/g, :] (and the matching rows of sb), the activations are
 replicated, and rank r computes out[:, r*N/g:(r+1)*N/g] with no exchange inside the
-GEMM. The only collective is the optional all-gather of the bf16 output
-(`torch.distributed.all_gather_into_tensor` over NCCL, i.e. NVLink/NVSwitch),
-which lands as [g, M, N/g] and is re-laid out to [M, N].
+GEMM. The only collective is the optional all-gather of the bf16 output: either
+`torch.distributed.all_gather_into_tensor` over NCCL (NVLink/NVSwitch), which lands as
+[g, M, N/g] and is re-laid out to [M, N], or, for decode batches, fused into the GEMM's
+epilogue (FusedGather: each rank's kernel stores its tiles straight into every rank's
+output over peer memory, then a flag barrier).
 
 One process per GPU; the process group comes from `torch.distributed`.
 """
@@ -68,4 +70,73 @@ def sharded_gemm(local_gemm: Callable[..., torch.Tensor], a, b_local, *, world: 
     return gather_columns(out_local, world, group=group)
 
 
-__all__ = ["column_range", "shard_weights", "shard_columns", "gather_columns", "sharded_gemm"]
+class FusedGather:
+    """Every rank's gathered output, mapped into this process, for the A8W4 decode GEMM
+    with the all-gather fused into its epilogue (`arc_a8w4_gemm_gather`).
+
+    Collective: every rank of `group` (one process per GPU, all GPUs of one node) builds
+    it with the same `m` and `n_total`. Each rank allocates its [m, n_total] bf16 output
+    and a small flag array, shares both with CUDA IPC (torch's handles, exchanged with
+    `all_gather_object`) and opens the others', so its GEMM can store its column block
+    into every rank's output over NVLink and `arc_peer_barrier` can tell when all blocks
+    have landed. `out` is this rank's gathered output; each `matmul` call overwrites it
+    (and the other ranks') with the next result.
+    """
+
+    def __init__(self, m: int, n_total: int, *, group=None, device: torch.device | None = None):
+        import ctypes
+
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("the fused all-gather spans at most 8 GPUs")
+        column_range(n_total, self.rank, self.world)  # validates the split
+        dev = device or torch.device("cuda", torch.cuda.current_device())
+        self.m, self.n_total = m, n_total
+        self.out = torch.zeros((m, n_total), dtype=torch.bfloat16, device=dev)
+        self.flags = torch.zeros(self.world, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        mine = (self.out.untyped_storage()._share_cuda_(), self.flags.untyped_storage()._share_cuda_())
+        handles = [None] * self.world
+        dist.all_gather_object(handles, mine, group=group)
+        self._opened = []  # keeps the peers' mappings alive
+        outs, flags = [], []
+        for i, (h_out, h_flags) in enumerate(handles):
+            if i == self.rank:
+                outs.append(self.out.data_ptr())
+                flags.append(self.flags.data_ptr())
+                continue
+            s_out = torch.UntypedStorage._new_shared_cuda(*h_out)
+            s_flags = torch.UntypedStorage._new_shared_cuda(*h_flags)
+            self._opened += [s_out, s_flags]
+            outs.append(s_out.data_ptr())
+            flags.append(s_flags.data_ptr())
+        self._outs = (ctypes.c_void_p * self.world)(*outs)
+        self._flags = (ctypes.c_void_p * self.world)(*flags)
+        self.epoch = 0
+        dist.barrier(group=group)  # every mapping exists before any rank writes into it
+
+    def matmul(self, a: TensorPair, b_local: TensorPair) -> torch.Tensor:
+        """This rank's column block of the A8W4 decode GEMM, stored into every rank's
+        output, then the barrier after which `out` holds all blocks."""
+        from ._lib import check, lib
+
+        x, sa = a
+        wp, sb = b_local
+        m, k = x.shape
+        n = wp.shape[0]
+        if m != self.m or n * self.world != self.n_total:
+            raise ValueError(f"shape [{m}, {n} x {self.world}] does not match this gather "
+                             f"[{self.m}, {self.n_total}]")
+        stream = torch.cuda.current_stream(self.out.device).cuda_stream
+        check(lib().arc_a8w4_gemm_gather(x.data_ptr(), sa.data_ptr(), wp.data_ptr(), sb.data_ptr(),
+                                         self._outs, self.world, self.rank, m, n, k, stream),
+              "arc_a8w4_gemm_gather")
+        self.epoch += 1
+        check(lib().arc_peer_barrier(self._flags, self.world, self.rank, self.epoch, stream),
+              "arc_peer_barrier")
+        return self.out
+
+
+__all__ = ["column_range", "shard_weights", "shard_columns", "gather_columns", "sharded_gemm",
+           "FusedGather"]

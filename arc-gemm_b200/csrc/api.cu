@@ -18,6 +18,8 @@
 #include "gemm_a8w4_decode.cuh"
 #include "gemm_fp8fp4.cuh"
 #include "gemm_fp8fp4_pair.cuh"
+#include "peer_barrier.cuh"
+#include "prepack.cuh"
 #include "quantize.cuh"
 #include "gemm_bf16.cuh"
 #include "sm100.cuh"
@@ -565,6 +567,9 @@ SplitPlan fp8fp4_split_plan(int dev, int M, int N, int K) {
 
 int fp8fp4_gemm(const uint8_t* A, const float* sfa, const uint8_t* Wp, const float* sfw, uint16_t* C,
                 int M, int N, int K, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+int a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_t* sb, uint16_t* C, int M,
+              int N, int K, int group, cudaStream_t stream, int32_t* partials_dbg, uint16_t* const* outs,
+              int world, int rank, uint32_t split);
 
 }  // namespace
 
@@ -722,6 +727,107 @@ int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uin
                   uint16_t* C, int M, int N, int K, int group, cudaStream_t stream,
                   int32_t* partials_dbg) {
   g_last_error[0] = '\0';
+  return a8w4_gemm(A, sa, Wp, sb, C, M, N, K, group, stream, partials_dbg, nullptr, 0, 0, 0u);
+}
+
+int arc_a8w4_gemm_prepacked(const int8_t* A, const float* sa, const uint8_t* Wq, const uint16_t* sb,
+                            uint16_t* C, int M, int N, int K, int group, cudaStream_t stream) {
+  g_last_error[0] = '\0';
+  return a8w4_gemm(A, sa, Wq, sb, C, M, N, K, group, stream, nullptr, nullptr, 0, 0, 1u);
+}
+
+int arc_a8w4_prepack_weights(const uint8_t* Wp, uint8_t* Wq, int N, int K, cudaStream_t stream) {
+  g_last_error[0] = '\0';
+  if (Wp == nullptr || Wq == nullptr) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_a8w4_prepack_weights: null pointer");
+  }
+  if (N <= 0 || K <= 0) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_a8w4_prepack_weights: sizes must be positive (N=%d K=%d)", N, K);
+  }
+  if (K % 32 != 0) {
+    return fail(ARC_ERR_UNSUPPORTED, "arc_a8w4_prepack_weights: K (%d) must be a multiple of 32", K);
+  }
+  if (!aligned16(Wp) || !aligned16(Wq)) {
+    return fail(ARC_ERR_UNSUPPORTED, "arc_a8w4_prepack_weights: Wp and Wq must be 16-byte aligned");
+  }
+  const uint64_t bytes = uint64_t(N) * uint64_t(K / 2);
+  const uintptr_t src = reinterpret_cast<uintptr_t>(Wp), dst = reinterpret_cast<uintptr_t>(Wq);
+  if (src != dst && src < dst + bytes && dst < src + bytes) {
+    return fail(ARC_ERR_INVALID_ARGUMENT,
+                "arc_a8w4_prepack_weights: Wq overlaps Wp without being the same buffer");
+  }
+  int dev = 0;
+  if (int st = current_device(&dev)) return st;
+  namespace PP = arcb::prepack;
+  const uint64_t pieces = bytes / 16u;
+  const uint64_t per_block = uint64_t(PP::kThreads) * PP::kUnroll;
+  const uint64_t want = (pieces + per_block - 1) / per_block;
+  const uint64_t cap = uint64_t(g_dev[dev].sms) * 8u;  // 8 resident 256-thread blocks per SM
+  const uint32_t grid = static_cast<uint32_t>(want < cap ? want : cap);
+  PP::prepack_w4_kernel<<<grid, PP::kThreads, 0, stream>>>(reinterpret_cast<const uint4*>(Wp),
+                                                           reinterpret_cast<uint4*>(Wq), pieces);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "prepack_w4_kernel launch");
+  return ARC_OK;
+}
+
+int arc_a8w4_gemm_gather(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_t* sb,
+                         uint16_t* const* outs, int world, int rank, int M, int N, int K,
+                         cudaStream_t stream) {
+  g_last_error[0] = '\0';
+  if (outs == nullptr || world < 1 || world > static_cast<int>(arcb::peer::kMaxPeers) || rank < 0 ||
+      rank >= world) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_a8w4_gemm_gather: bad outs / world (%d) / rank (%d)", world,
+                rank);
+  }
+  for (int i = 0; i < world; ++i) {
+    if (outs[i] == nullptr || !aligned16(outs[i])) {
+      return fail(ARC_ERR_INVALID_ARGUMENT, "arc_a8w4_gemm_gather: output %d is null or not 16-byte aligned", i);
+    }
+  }
+  if (M <= 0 || M > static_cast<int>(kDecodeMaxM)) {
+    return fail(ARC_ERR_UNSUPPORTED,
+                "arc_a8w4_gemm_gather: the fused all-gather covers decode batches (1 <= M <= %u, got %d)",
+                kDecodeMaxM, M);
+  }
+  if (N <= 0 || N % 8 != 0) {
+    return fail(ARC_ERR_UNSUPPORTED, "arc_a8w4_gemm_gather: N (%d) must be a positive multiple of 8", N);
+  }
+  return a8w4_gemm(A, sa, Wp, sb, outs[rank] + size_t(rank) * N, M, N, K, 128, stream, nullptr, outs, world,
+                   rank, 0u);
+}
+
+int arc_peer_barrier(uint32_t* const* flags, int world, int rank, uint32_t epoch, cudaStream_t stream) {
+  g_last_error[0] = '\0';
+  if (flags == nullptr || world < 1 || world > static_cast<int>(arcb::peer::kMaxPeers) || rank < 0 ||
+      rank >= world) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_peer_barrier: bad flags / world (%d) / rank (%d)", world, rank);
+  }
+  arcb::peer::BarrierParams b = {};
+  for (int i = 0; i < world; ++i) {
+    if (flags[i] == nullptr || (reinterpret_cast<uintptr_t>(flags[i]) & 3u)) {
+      return fail(ARC_ERR_INVALID_ARGUMENT, "arc_peer_barrier: flag array %d is null or misaligned", i);
+    }
+    b.flags[i] = flags[i];
+  }
+  b.world = static_cast<uint32_t>(world);
+  b.rank = static_cast<uint32_t>(rank);
+  b.epoch = epoch;
+  int dev = 0;
+  if (int st = current_device(&dev)) return st;
+  arcb::peer::peer_barrier_kernel<<<1, 32, 0, stream>>>(b);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "peer_barrier_kernel launch");
+  return ARC_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+int a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_t* sb, uint16_t* C, int M,
+              int N, int K, int group, cudaStream_t stream, int32_t* partials_dbg, uint16_t* const* outs,
+              int world, int rank, uint32_t split) {
   if (A == nullptr || sa == nullptr || Wp == nullptr || sb == nullptr || C == nullptr) {
     return fail(ARC_ERR_INVALID_ARGUMENT, "arc_a8w4_gemm: null pointer");
   }
@@ -765,9 +871,24 @@ int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uin
       return st;
     }
     const uint32_t S = static_cast<uint32_t>(plan.k_split);
-    if (int st = encode_2d(&p.tm_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, N, M, N, R / S, BT,
+    // The output: C [M][N], or with a fused all-gather this rank's [M][N] column window of
+    // every rank's [M][world*N] output (row pitch world*N).
+    const uint32_t ldo = outs != nullptr ? static_cast<uint32_t>(N * world) : static_cast<uint32_t>(N);
+    if (int st = encode_2d(&p.tm_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C, N, M, ldo, R / S, BT,
                            CU_TENSOR_MAP_SWIZZLE_NONE, "C")) {
       return st;
+    }
+    p.peers = 0;
+    p.split = split;
+    if (outs != nullptr) {
+      for (int i = 0; i < world; ++i) {
+        if (int st = encode_2d(&p.tm_peer[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                               outs[i] + size_t(rank) * N, N, M, ldo, R / S, BT, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               "peer output")) {
+          return st;
+        }
+      }
+      p.peers = static_cast<uint32_t>(world);
     }
     p.sa = sa;
     p.sb = sb;
@@ -778,7 +899,7 @@ int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uin
     p.K = K;
     p.G = G;
     p.ldsb = G;
-    p.ldc = N;
+    p.ldc = ldo;
     p.R = R;
     p.S = plan.k_split;
     p.num_items = ceil_div(N, R);
@@ -826,6 +947,7 @@ int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uin
   p.tiles_m = ceil_div(M, BT);
   p.tiles_n = ceil_div(N, R);
   p.num_tiles = p.tiles_m * p.tiles_n;
+  p.split = split;
   const uint32_t grid = static_cast<uint32_t>(plan.grid);
   if (BT == 64) {
     e = launch_ex(Q::gemm_a8w4_kernel<64, 1, 4>, p, grid, Q::Cfg<64, 1, 4>::kThreads,
@@ -837,6 +959,10 @@ int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uin
   if (e != cudaSuccess) return cuda_fail(e, "gemm_a8w4_kernel launch");
   return ARC_OK;
 }
+
+}  // namespace
+
+extern "C" {
 
 int arc_fp8_fp4_gemm(const uint8_t* A, const float* sfa, const uint8_t* Wp, const float* sfw,
                      uint16_t* C, int M, int N, int K, cudaStream_t stream) {

@@ -93,6 +93,7 @@ struct Params {
   uint32_t ldc;        // elements between out rows
   uint32_t R;          // weight rows per tile (128)
   uint32_t tiles_m, tiles_n, num_tiles;
+  uint32_t split;      // Wp in the pre-packed layout (expand_piece)
 };
 
 template <uint32_t BT, uint32_t EWG, uint32_t LS>
@@ -176,6 +177,24 @@ __device__ __forceinline__ uint2 expand_int4x8(uint32_t x) {
   const uint32_t even = (x << 4) & 0xF0F0F0F0u;  // byte j: code k=2j   in bits 7:4
   const uint32_t odd = x & 0xF0F0F0F0u;          // byte j: code k=2j+1 in bits 7:4
   return make_uint2(__byte_perm(even, odd, 0x5140), __byte_perm(even, odd, 0x7362));
+}
+
+// One 16-byte piece of a weight row (32 codes, k = 32q .. 32q+31) -> its 32 int8 codes
+// (16*w) as two 16-byte chunks, k ascending: lo = k 0..15, hi = k 16..31.
+// split == 0: the reference's packing (byte j = codes 2j | 2j+1 << 4).
+// split != 0: the pre-packed layout (byte j = codes j | j+16 << 4, arc_a8w4_prepack_weights),
+// where both chunks are a mask (and a shift) of the piece, with no byte permutes.
+__device__ __forceinline__ void expand_piece(const uint4& x, uint32_t split, uint4& lo, uint4& hi) {
+  if (split) {
+    lo = make_uint4((x.x << 4) & 0xF0F0F0F0u, (x.y << 4) & 0xF0F0F0F0u, (x.z << 4) & 0xF0F0F0F0u,
+                    (x.w << 4) & 0xF0F0F0F0u);
+    hi = make_uint4(x.x & 0xF0F0F0F0u, x.y & 0xF0F0F0F0u, x.z & 0xF0F0F0F0u, x.w & 0xF0F0F0F0u);
+  } else {
+    const uint2 a = expand_int4x8(x.x), b = expand_int4x8(x.y);
+    const uint2 c = expand_int4x8(x.z), d = expand_int4x8(x.w);
+    lo = make_uint4(a.x, a.y, b.x, b.y);
+    hi = make_uint4(c.x, c.y, d.x, d.y);
+  }
 }
 
 // ---------------------------------------------------------------------------------
@@ -375,12 +394,11 @@ __global__ void __launch_bounds__(Cfg<BT, EWG, LS>::kThreads, 1)
 #pragma unroll
         for (uint32_t i = 0; i < 8; ++i) {
           const uint32_t r = (i & 3u) * 32u + (ut >> 2);
-          const uint2 a = expand_int4x8(x[i].x), b = expand_int4x8(x[i].y);
-          const uint2 c = expand_int4x8(x[i].z), d = expand_int4x8(x[i].w);
+          uint4 lo, hi;
+          expand_piece(x[i], p.split, lo, hi);
           uint8_t* row = s.w[us][i >> 2] + r * kGroupK;
-          *reinterpret_cast<uint4*>(row + (((2u * c16) ^ (r & 7u)) << 4)) = make_uint4(a.x, a.y, b.x, b.y);
-          *reinterpret_cast<uint4*>(row + (((2u * c16 + 1u) ^ (r & 7u)) << 4)) =
-              make_uint4(c.x, c.y, d.x, d.y);
+          *reinterpret_cast<uint4*>(row + (((2u * c16) ^ (r & 7u)) << 4)) = lo;
+          *reinterpret_cast<uint4*>(row + (((2u * c16 + 1u) ^ (r & 7u)) << 4)) = hi;
         }
         fence_proxy_async_smem();
         __syncwarp();

@@ -38,7 +38,7 @@
 namespace arcb {
 namespace a8w4dec {
 
-using a8w4::expand_int4x8;
+using a8w4::expand_piece;
 using a8w4::kGroupK;
 using a8w4::kPackedRow;
 using a8w4::kRows;
@@ -52,6 +52,7 @@ constexpr uint32_t kRingBytes = 88 * 1024;
 constexpr uint32_t kSlotBytes = 112 * 1024;  // unpacked slots, R*128 bytes apart
 constexpr uint32_t kMaxSlots = 16;
 constexpr uint32_t kScaleLookahead = 8;
+constexpr uint32_t kMaxPeers = 8;  // GPUs of a fused all-gather
 
 struct Params {
   CUtensorMap tm_tok;  // A as [G][M][128] u8 (3-D), box {128, BT, GPS}, SW128
@@ -72,6 +73,12 @@ struct Params {
   uint32_t tok_bytes;  // token part of a stage: gps * BT * 128
   uint32_t slots;      // unpacked slots (<= kMaxSlots)
   uint32_t slot_stride;  // R * 128 (a multiple of 1024)
+  // Fused all-gather (peers > 0): every output tile is stored into each rank's output
+  // through tm_peer[i], the [M][N] column window of rank i's gathered [M][world*N] output
+  // that this rank owns (peer memory over NVLink; TMA stores only). tm_out is then unused.
+  uint32_t peers;
+  uint32_t split;  // Wp in the pre-packed layout (a8w4::expand_piece)
+  CUtensorMap tm_peer[kMaxPeers];
 };
 
 template <uint32_t BT>
@@ -133,15 +140,6 @@ __device__ __forceinline__ void st_dsmem_f32x4(uint32_t addr, float a, float b, 
   asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b),
                "f"(c), "f"(d)
                : "memory");
-}
-
-// 16 packed bytes (32 int4, k ascending, even k in the low nibbles) -> 32 int8 codes
-// (16*w) as two 16-byte chunks.
-__device__ __forceinline__ void expand_int4x32(const uint4& x, uint4& lo, uint4& hi) {
-  const uint2 a = expand_int4x8(x.x), b = expand_int4x8(x.y);
-  const uint2 c = expand_int4x8(x.z), d = expand_int4x8(x.w);
-  lo = make_uint4(a.x, a.y, b.x, b.y);
-  hi = make_uint4(c.x, c.y, d.x, d.y);
 }
 
 template <uint32_t BT>
@@ -343,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (uint32_t r = row0; r < p.R; r += row_step) {
             const uint4 x = *reinterpret_cast<const uint4*>(packed + r * row_bytes + piece * 16u);
             uint4 lo, hi;
-            expand_int4x32(x, lo, hi);
+            expand_piece(x, p.split, lo, hi);
             uint8_t* dst = slot + r * kGroupK;
             const uint32_t sw = r & 7u;
             *reinterpret_cast<uint4*>(dst + (((2u * quarter) ^ sw) << 4)) = lo;
@@ -453,7 +451,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_smem();
         named_barrier_sync(1, 128);
         if (et == 0 && *abort == 0u) {
-          tma_store_2d(&p.tm_out, tile, int32_t(it.n0), 0);
+          if (p.peers == 0) {
+            tma_store_2d(&p.tm_out, tile, int32_t(it.n0), 0);
+          } else {
+            for (uint32_t i = 0; i < p.peers; ++i) tma_store_2d(&p.tm_peer[i], tile, int32_t(it.n0), 0);
+          }
           tma_store_commit();
         }
       } else {
@@ -508,7 +510,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_smem();
         named_barrier_sync(1, 128);
         if (et == 0 && *abort == 0u) {
-          tma_store_2d(&p.tm_out, tile, int32_t(it.n0 + rank * rows_per), 0);
+          if (p.peers == 0) {
+            tma_store_2d(&p.tm_out, tile, int32_t(it.n0 + rank * rows_per), 0);
+          } else {
+            for (uint32_t i = 0; i < p.peers; ++i) {
+              tma_store_2d(&p.tm_peer[i], tile, int32_t(it.n0 + rank * rows_per), 0);
+            }
+          }
           tma_store_commit();
           probe_mark(6);  // output store issued
         }

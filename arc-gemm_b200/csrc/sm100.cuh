@@ -35,6 +35,7 @@ enum : uint32_t {
   kStatusTimeoutEpilogue = 1u << 3,
   kStatusTimeoutDrain = 1u << 4,
   kStatusTimeoutScales = 1u << 5,
+  kStatusTimeoutPeer = 1u << 6,
 };
 
 // One word per loaded module; every kernel in this translation unit ORs into it.

@@ -1,7 +1,8 @@
 """Benchmark of the arc A8W4 GEMM on B200 (the BASELINE metric).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|prefill|bf16_2048|bf16_8192] [--allgather]
+                    [--workload decode|prefill|bf16_2048|bf16_8192]
+                    [--allgather [nccl|fused]] [--prepacked]
 
 Prints ONE JSON line on rank 0.
 
@@ -10,7 +11,9 @@ activations with per-token fp32 scales, int4 weights packed two per byte with bf
 per-(column, 128-group) scales, bf16 output; seeded synthetic data. A step is one
 GEMM over one batch. With N GPUs each rank owns its own 4096-column slice of an
 N*4096-column weight (weak scaling, no collective in the data path; `--allgather`
-adds the NCCL all-gather of the output).
+adds the NCCL all-gather of the output, `--allgather fused` the all-gather fused into
+the decode GEMM's epilogue). `--prepacked` runs the A8W4 GEMM on weights converted once,
+before timing, by arc.prepack_weights.
 
 Timing: W untimed warm-up steps, then exactly K steps between barrier +
 synchronize on both sides, on the launching stream with CUDA events, max over ranks.
@@ -320,7 +323,7 @@ def run_ours(args, wl, world, rank, local):
         in_bytes = step_bytes - 2 * M * N
 
         def call(s):
-            return arc.a8w4_matmul(s[0], s[1], s[2])
+            return arc.a8w4_matmul(s[0], s[1], s[2], prepacked=args.prepacked)
     elif wl["kind"] == "fp8fp4":
         step_bytes = fp8fp4_bytes(M, N, K)
         in_bytes = step_bytes - 2 * M * N
@@ -337,11 +340,28 @@ def run_ours(args, wl, world, rank, local):
     # Enough distinct input sets that consecutive steps never find theirs in L2.
     n_sets = max(1, min(64, -(-2 * L2_BYTES // in_bytes)))
     sets = build_inputs(wl, rank, device, n_sets)
+    if args.prepacked:
+        if wl["kind"] != "a8w4":
+            raise SystemExit("--prepacked applies to the A8W4 workloads")
+        # One-time weight format step, outside the timed region; its own kernel time is
+        # reported beside the line (in place, one call per input set, HBM-bound).
+        arc.prepack_weights(sets[0][1][0])  # untimed first call (library and module setup)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in sets]
+        for st, (e0, e1) in zip(sets, evs):
+            e0.record()
+            arc.prepack_weights(st[1][0], out=st[1][0])
+            e1.record()
+        torch.cuda.synchronize(device)
+        pp_us = sum(e0.elapsed_time(e1) for e0, e1 in evs) * 1e3 / len(sets)
+        pp_bytes = 2 * N * K // 2  # every packed byte read once and written once
+        prepack_info = {"us_per_call": pp_us, "bytes_per_call": pp_bytes,
+                        "gbs": pp_bytes / (pp_us * 1e-6) / 1e9, "calls": len(sets)}
     flush = None
     if n_sets == 1:  # inputs alone exceed 2x L2 only for the large configs
         flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.int32, device=device)
-    gather = args.allgather and world > 1
-    if gather:
+    gather = args.allgather if world > 1 else None
+    launches_per_step = 1
+    if gather == "nccl":
         # Each step also all-gathers the bf16 output over NCCL into [world*M, N/world]
         # (arc.parallel.gather_columns' layout); eager launches, no graph.
         import torch.distributed as dist
@@ -353,6 +373,19 @@ def run_ours(args, wl, world, rank, local):
             out = local_call(s)
             dist.all_gather_into_tensor(gathered, out)
             return gathered
+    elif gather == "fused":
+        # The GEMM stores its tiles into every rank's [M, world*N] output over NVLink,
+        # then a flag barrier (arc.parallel.FusedGather); eager launches, no graph.
+        if wl["kind"] != "a8w4" or M > 32 or args.prepacked:
+            raise SystemExit("--allgather fused covers the A8W4 decode workload (M <= 32, "
+                             "reference packing)")
+        from arc import parallel as par
+
+        fused = par.FusedGather(M, world * N, device=device)
+        launches_per_step = 2
+
+        def call(s):
+            return fused.matmul(s[0], s[1])
     use_graph = flush is None and not args.no_graph and not gather
     stream = torch.cuda.Stream(device)
     peaks = load_peaks()
@@ -463,8 +496,12 @@ def run_ours(args, wl, world, rank, local):
                            (n_sets, n_sets * in_bytes / 1e6)) if flush is None
                        else "L2 flushed (512 MB write) before every timed step",
                        launch="K launches in one CUDA graph" if use_graph else "eager launches",
-                       allgather=("NCCL all_gather_into_tensor of the bf16 output every step"
-                                  if gather else False)),
+                       allgather={"nccl": "NCCL all_gather_into_tensor of the bf16 output every step",
+                                  "fused": "fused into the GEMM epilogue: TMA stores of every tile "
+                                           "into each rank's output over NVLink + a flag barrier"
+                                  }.get(gather, False),
+                       weights_layout=("pre-packed (arc.prepack_weights, outside the timed region)"
+                                       if args.prepacked else "reference packing")),
         "hbm_gbs": world * step_bytes / (step_ms * 1e-3) / 1e9,
         "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                      "frac": achieved / peak, "traffic": traffic,
@@ -475,7 +512,9 @@ def run_ours(args, wl, world, rank, local):
                 "unit": "TOPS" if wl["kind"] == "a8w4" else "TFLOP/s",
                 "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
                 "ms_per_step": e2e_ms},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * launches_per_step,
+        **({"prepack": dict(prepack_info, frac=prepack_info["gbs"] / peaks["hbm_gbs"])}
+           if args.prepacked else {}),
         "clocks": clk,
     }
     if world == 1 and wl["kind"] == "a8w4" and not args.skip_cpu_baseline:
@@ -504,7 +543,8 @@ def run_e2e(args, wl, s, device, stream, world):
             for h, d in zip(host, dev_bufs):
                 d.copy_(h, non_blocking=True)
             if wl["kind"] == "a8w4":
-                o = arc.a8w4_matmul((dev_bufs[0], dev_bufs[1]), (dev_bufs[2], dev_bufs[3]))
+                o = arc.a8w4_matmul((dev_bufs[0], dev_bufs[1]), (dev_bufs[2], dev_bufs[3]),
+                                    prepacked=args.prepacked)
             else:
                 o = arc.fp8_fp4_gemm_nt((dev_bufs[0], dev_bufs[1]), (dev_bufs[2], dev_bufs[3]), out_d)
             out_h.copy_(o, non_blocking=True)
@@ -542,7 +582,9 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=tuple(WORKLOADS), default="decode")
-    ap.add_argument("--allgather", action="store_true")
+    ap.add_argument("--allgather", nargs="?", const="nccl", choices=("nccl", "fused"), default=None)
+    ap.add_argument("--prepacked", action="store_true",
+                    help="A8W4: weights converted once by arc.prepack_weights before timing")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--settle-s", type=float, default=1.0)
     ap.add_argument("--cpu-budget-s", type=float, default=10.0)

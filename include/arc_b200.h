@@ -89,6 +89,25 @@ int arc_a8w4_gemm(const int8_t *A, const float *sa, const uint8_t *Wp, const uin
                   uint16_t *C, int M, int N, int K, int group, cudaStream_t stream,
                   int32_t *partials_dbg);
 
+/*
+ * Weight pre-pack (no reference counterpart: the reference stores weights only in the
+ * packing of arc/testing/quant.py:82-83, which Wp above follows). Reorders the nibbles
+ * inside every 16-byte piece of Wp [N][K/2] (32 codes, k = 32q .. 32q+31) so that byte j
+ * holds code 32q+j in bits 3:0 and code 32q+j+16 in bits 7:4. Shape, size and strides
+ * are unchanged. Wq may be Wp itself (in place); any other overlap is rejected. Runs on
+ * `stream`, reading and writing N*K/2 bytes once. Requirements: K % 32 == 0; Wp, Wq
+ * 16-byte aligned.
+ */
+int arc_a8w4_prepack_weights(const uint8_t *Wp, uint8_t *Wq, int N, int K, cudaStream_t stream);
+
+/*
+ * arc_a8w4_gemm on weights in the pre-packed layout (arc_a8w4_prepack_weights). Same
+ * arithmetic, results bit-identical to arc_a8w4_gemm on the original Wp; the kernels'
+ * int4 -> int8 expansion is a mask and shift instead of byte permutes. No partials dump.
+ */
+int arc_a8w4_gemm_prepacked(const int8_t *A, const float *sa, const uint8_t *Wq, const uint16_t *sb,
+                            uint16_t *C, int M, int N, int K, int group, cudaStream_t stream);
+
 /* The work decomposition arc_a8w4_gemm picks for a shape (host-only, no GPU needed). */
 typedef struct arc_a8w4_plan {
   int split;        /* 1: K-split clusters with on-chip reduction; 0: persistent tiles */
@@ -101,6 +120,30 @@ typedef struct arc_a8w4_plan {
 } arc_a8w4_plan_t;
 
 int arc_a8w4_describe_plan(int M, int N, int K, int num_sms, arc_a8w4_plan_t *plan);
+
+/*
+ * A8W4 decode GEMM with the all-gather of its output fused into the epilogue (the
+ * multi-GPU step after the reference's single-GPU call, tests/a8w4.py:48: one process
+ * per GPU, weight columns sharded). Rank `rank` of `world` (<= 8) holds the weight
+ * columns [rank*N, (rank+1)*N) (Wp [N][K/2], sb [N][K/128]); outs[i] is rank i's full
+ * output [M][world*N] bf16, mapped into this process (CUDA IPC). Every output tile is
+ * stored by TMA straight into all `world` outputs over NVLink, so no separate gather
+ * runs. Decode batches only (1 <= M <= 32); other arguments as arc_a8w4_gemm. The
+ * other ranks' writes into this rank's output are complete only after
+ * arc_peer_barrier; a call overwrites the output of the previous one on every rank.
+ */
+int arc_a8w4_gemm_gather(const int8_t *A, const float *sa, const uint8_t *Wp, const uint16_t *sb,
+                         uint16_t *const *outs, int world, int rank, int M, int N, int K,
+                         cudaStream_t stream);
+
+/*
+ * Stream-ordered barrier of the ranks of a fused all-gather: announces `epoch` in every
+ * rank's flag array (flags[i]: rank i's `world` uint32 flags, zeroed once, mapped into
+ * this process) and waits on `stream` until this rank's array holds an epoch >= `epoch`
+ * from every rank. Epochs must grow by one per call, in the same order on every rank.
+ * The wait gives up after 2 s and reports it through arc_device_status.
+ */
+int arc_peer_barrier(uint32_t *const *flags, int world, int rank, uint32_t epoch, cudaStream_t stream);
 
 /*
  * FP8 x FP4 GEMM with UE8M0 block scales, the recipe of the reference's A8W4 test

@@ -131,6 +131,34 @@ def np_unpack_int4(packed: np.ndarray) -> np.ndarray:
     return np.where(codes >= 8, codes - 16, codes).astype(np.int8)
 
 
+def np_prepack_int4(packed: np.ndarray) -> np.ndarray:
+    """The reference's packing -> the pre-packed layout of arc_a8w4_prepack_weights.
+
+    The reference has no pre-pack; this restates the layout that entry point defines on
+    top of the reference's nibble order (arc/testing/quant.py:82-83): inside every
+    16-byte piece of a row (32 codes, k = 32q .. 32q+31), byte j = code j in bits 3:0 and
+    code j+16 in bits 7:4 (codes as raw 4-bit patterns).
+    """
+    p = np.asarray(packed, dtype=np.uint8)
+    n, kb = p.shape
+    assert kb % 16 == 0, "K must be a multiple of 32"
+    nib = np.empty((n, 2 * kb), dtype=np.uint8)
+    nib[:, 0::2] = p & 0x0F
+    nib[:, 1::2] = p >> 4
+    nib = nib.reshape(n, kb // 16, 32)
+    return (nib[..., :16] | (nib[..., 16:] << 4)).reshape(n, kb)
+
+
+def np_unprepack_int4(prepacked: np.ndarray) -> np.ndarray:
+    """Inverse of np_prepack_int4: the pre-packed layout -> the reference's packing."""
+    q = np.asarray(prepacked, dtype=np.uint8)
+    n, kb = q.shape
+    assert kb % 16 == 0, "K must be a multiple of 32"
+    pieces = q.reshape(n, kb // 16, 16)
+    nib = np.concatenate([pieces & 0x0F, pieces >> 4], axis=-1).reshape(n, 2 * kb)
+    return (nib[:, 0::2] | (nib[:, 1::2] << 4)).astype(np.uint8)
+
+
 def np_a8w4_partials(a: np.ndarray, w_packed: np.ndarray, group: int = 128) -> np.ndarray:
     """Independent numpy partials via int64 matmul per group."""
     w = np_unpack_int4(w_packed).astype(np.int64)

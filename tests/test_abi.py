@@ -69,6 +69,18 @@ def test_invalid_arguments_are_rejected_before_any_cuda_call(native_lib):
     a32 = (p + 31) // 32 * 32  # 32-byte aligned inside the buffer
     assert L.arc_fp8_fp4_gemm(a32, a32, a32 + 16, a32, a32, 16, 64, 256, nul) == \
         _lib.ARC_ERR_UNSUPPORTED
+    # weight pre-pack: K not a multiple of 32, misaligned, partial overlap; prepacked GEMM group
+    assert L.arc_a8w4_prepack_weights(p, p, 4, 48, nul) == _lib.ARC_ERR_UNSUPPORTED
+    assert L.arc_a8w4_prepack_weights(p + 1, p + 1, 4, 64, nul) == _lib.ARC_ERR_UNSUPPORTED
+    assert L.arc_a8w4_prepack_weights(a32, a32 + 16, 4, 64, nul) == _lib.ARC_ERR_INVALID_ARGUMENT
+    assert L.arc_a8w4_prepack_weights(nul, p, 4, 64, nul) == _lib.ARC_ERR_INVALID_ARGUMENT
+    assert L.arc_a8w4_gemm_prepacked(p, p, p, p, p, 16, 64, 256, 64, nul) == _lib.ARC_ERR_UNSUPPORTED
+    # fused all-gather: world out of range, prefill-sized M; peer barrier: rank >= world
+    outs = (ctypes.c_void_p * 2)(a32, a32)
+    assert L.arc_a8w4_gemm_gather(p, p, p, p, outs, 9, 0, 16, 64, 256, nul) == \
+        _lib.ARC_ERR_INVALID_ARGUMENT
+    assert L.arc_a8w4_gemm_gather(p, p, p, p, outs, 2, 0, 64, 64, 256, nul) == _lib.ARC_ERR_UNSUPPORTED
+    assert L.arc_peer_barrier(outs, 2, 2, 1, nul) == _lib.ARC_ERR_INVALID_ARGUMENT
     # kernel-name query: no buffer / non-positive sizes
     assert L.arc_kernel_name(0, 8, 8, 8, nul, 16) == _lib.ARC_ERR_INVALID_ARGUMENT
     assert L.arc_kernel_name(0, 0, 8, 8, ctypes.cast(buf, ctypes.c_char_p), 16) == \

@@ -75,3 +75,62 @@ def test_two_gpu_sharded_gemm_with_all_gather(m, n, k):
                 p.kill()
     assert ok, "sharded + gathered output differs from the single-GPU GEMM"
     assert all(p.exitcode == 0 for p in procs)
+
+
+def _fused_worker(rank, world, port, m, n, k, result_q):
+    """Each rank: its column block through the GEMM with the fused all-gather, twice in a
+    row (two barrier epochs); the gathered output must equal the NCCL all-gather of the
+    same blocks bit for bit (same kernel, same plan per block)."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    sys.path[:0] = [str(root / "arc-gemm_b200"), str(root)]
+    import arc
+    from arc import parallel as par
+    from arc.testing.data import generate_a8w4
+
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        fg = par.FusedGather(m, n, device=dev)
+        ok = True
+        for seed in (5, 6):
+            (x, sa), (wp, sb) = generate_a8w4(m, n, k, seed=seed)
+            a = (x.to(dev), sa.to(dev))
+            b_local = par.shard_weights((wp.to(dev), sb.to(dev)), rank, world)
+            ref = par.sharded_gemm(arc.a8w4_matmul, a, b_local, world=world, all_gather=True)
+            got = fg.matmul(a, b_local)
+            torch.cuda.synchronize()
+            ok = ok and bool(torch.equal(got, ref)) and arc.device_status(rank) == 0
+            dist.barrier()
+        result_q.put((rank, ok))
+        dist.barrier()
+        del fg
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("m,n,k", [(16, 4096, 4096), (5, 1040, 1024)])
+def test_two_gpu_fused_all_gather(m, n, k):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, m, n, k, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        results = dict(q.get(timeout=240) for _ in range(world))
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    assert all(results.values()), f"fused all-gather differs from the NCCL all-gather: {results}"
+    assert all(p.exitcode == 0 for p in procs)
