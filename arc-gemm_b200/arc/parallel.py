@@ -70,47 +70,86 @@ def sharded_gemm(local_gemm: Callable[..., torch.Tensor], a, b_local, *, world: 
     return gather_columns(out_local, world, group=group)
 
 
+# Peer mappings opened by this process, by handle: a process may open each exported
+# allocation only once, so FusedGather objects that map the same peer segment share it.
+_OPENED: dict[bytes, list] = {}  # handle -> [mapping base, users]
+
+
+def _ipc_open(handle: bytes, offset: int) -> tuple[int, bytes]:
+    import ctypes
+
+    from ._lib import check, lib
+
+    entry = _OPENED.get(handle)
+    if entry is None:
+        ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
+        check(lib().arc_ipc_open(handle, 0, ctypes.byref(ptr), ctypes.byref(base)), "arc_ipc_open")
+        entry = _OPENED[handle] = [base.value, 0]
+    entry[1] += 1
+    return entry[0] + offset, handle
+
+
+def _ipc_close(handle: bytes) -> None:
+    from ._lib import check, lib
+
+    entry = _OPENED[handle]
+    entry[1] -= 1
+    if entry[1] == 0:
+        del _OPENED[handle]
+        check(lib().arc_ipc_close(entry[0]), "arc_ipc_close")
+
+
 class FusedGather:
     """Every rank's gathered output, mapped into this process, for the A8W4 decode GEMM
     with the all-gather fused into its epilogue (`arc_a8w4_gemm_gather`).
 
-    Collective: every rank of `group` (one process per GPU, all GPUs of one node) builds
-    it with the same `m` and `n_total`. Each rank allocates its [m, n_total] bf16 output
-    and a small flag array, shares both with CUDA IPC (torch's handles, exchanged with
-    `all_gather_object`) and opens the others', so its GEMM can store its column block
-    into every rank's output over NVLink and `arc_peer_barrier` can tell when all blocks
-    have landed. `out` is this rank's gathered output; each `matmul` call overwrites it
-    (and the other ranks') with the next result.
+    Collective: every rank of `group` (one process per GPU, all GPUs of one node, each
+    process seeing every GPU with the same numbering) builds it with the same `m` and
+    `n_total`. Each rank allocates one buffer holding its [m, n_total] bf16 output and a
+    small flag array, exports it with CUDA IPC (`arc_ipc_export`, handles exchanged with
+    `all_gather_object`) and maps the others' into its own GPU's context (`arc_ipc_open`,
+    which enables peer access from this GPU), so its GEMM can store its column block into
+    every rank's output over NVLink and `arc_peer_barrier` can tell when all blocks have
+    landed. `out` is this rank's gathered output; each `matmul` call overwrites it (and
+    the other ranks') with the next result. `close()` (collective) unmaps the peers.
     """
 
     def __init__(self, m: int, n_total: int, *, group=None, device: torch.device | None = None):
         import ctypes
 
+        from ._lib import check, lib
+
+        self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         if self.world > 8:
             raise ValueError("the fused all-gather spans at most 8 GPUs")
         column_range(n_total, self.rank, self.world)  # validates the split
-        dev = device or torch.device("cuda", torch.cuda.current_device())
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.m, self.n_total = m, n_total
-        self.out = torch.zeros((m, n_total), dtype=torch.bfloat16, device=dev)
-        self.flags = torch.zeros(self.world, dtype=torch.int32, device=dev)
-        torch.cuda.synchronize(dev)
-        mine = (self.out.untyped_storage()._share_cuda_(), self.flags.untyped_storage()._share_cuda_())
+        out_bytes = -(-m * n_total * 2 // 256) * 256
+        self._buf = torch.zeros(out_bytes + 256, dtype=torch.uint8, device=self.device)
+        self.out = self._buf[: m * n_total * 2].view(torch.bfloat16).view(m, n_total)
+        self.flags = self._buf[out_bytes: out_bytes + 4 * self.world].view(torch.int32)
+        torch.cuda.synchronize(self.device)
+        handle = ctypes.create_string_buffer(64)
+        offset = ctypes.c_uint64()
+        with torch.cuda.device(self.device):
+            check(lib().arc_ipc_export(self._buf.data_ptr(), handle, ctypes.byref(offset)), "arc_ipc_export")
+        mine = (handle.raw, offset.value)
         handles = [None] * self.world
         dist.all_gather_object(handles, mine, group=group)
-        self._opened = []  # keeps the peers' mappings alive
+        self._held = []  # peer handles this object opened
         outs, flags = [], []
-        for i, (h_out, h_flags) in enumerate(handles):
-            if i == self.rank:
-                outs.append(self.out.data_ptr())
-                flags.append(self.flags.data_ptr())
-                continue
-            s_out = torch.UntypedStorage._new_shared_cuda(*h_out)
-            s_flags = torch.UntypedStorage._new_shared_cuda(*h_flags)
-            self._opened += [s_out, s_flags]
-            outs.append(s_out.data_ptr())
-            flags.append(s_flags.data_ptr())
+        with torch.cuda.device(self.device):
+            for i, (h, off) in enumerate(handles):
+                if i == self.rank:
+                    base = self._buf.data_ptr()
+                else:
+                    base, key = _ipc_open(h, off)
+                    self._held.append(key)
+                outs.append(base)
+                flags.append(base + out_bytes)
         self._outs = (ctypes.c_void_p * self.world)(*outs)
         self._flags = (ctypes.c_void_p * self.world)(*flags)
         self.epoch = 0
@@ -128,14 +167,31 @@ class FusedGather:
         if m != self.m or n * self.world != self.n_total:
             raise ValueError(f"shape [{m}, {n} x {self.world}] does not match this gather "
                              f"[{self.m}, {self.n_total}]")
-        stream = torch.cuda.current_stream(self.out.device).cuda_stream
-        check(lib().arc_a8w4_gemm_gather(x.data_ptr(), sa.data_ptr(), wp.data_ptr(), sb.data_ptr(),
-                                         self._outs, self.world, self.rank, m, n, k, stream),
-              "arc_a8w4_gemm_gather")
-        self.epoch += 1
-        check(lib().arc_peer_barrier(self._flags, self.world, self.rank, self.epoch, stream),
-              "arc_peer_barrier")
+        for t in (x, sa, wp, sb):
+            if t.device != self.device:
+                raise ValueError(f"operand on {t.device}, expected {self.device}")
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        with torch.cuda.device(self.device):
+            check(lib().arc_a8w4_gemm_gather(x.data_ptr(), sa.data_ptr(), wp.data_ptr(), sb.data_ptr(),
+                                             self._outs, self.world, self.rank, m, n, k, stream),
+                  "arc_a8w4_gemm_gather")
+            self.epoch += 1
+            check(lib().arc_peer_barrier(self._flags, self.world, self.rank, self.epoch, stream),
+                  "arc_peer_barrier")
         return self.out
+
+    def close(self) -> None:
+        """Collective: wait for this GPU's work, unmap the peers' buffers, and let every
+        rank pass only once all ranks have unmapped (so no buffer is freed while mapped)."""
+        if self._held is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # no rank still writes into a peer buffer
+        with torch.cuda.device(self.device):
+            for key in self._held:
+                _ipc_close(key)
+        self._held = None
+        dist.barrier(group=self.group)
 
 
 __all__ = ["column_range", "shard_weights", "shard_columns", "gather_columns", "sharded_gemm",

@@ -797,6 +797,61 @@ int arc_a8w4_gemm_gather(const int8_t* A, const float* sa, const uint8_t* Wp, co
                    rank, 0u);
 }
 
+int arc_ipc_export(const void* ptr, void* handle, uint64_t* offset) {
+  g_last_error[0] = '\0';
+  if (ptr == nullptr || handle == nullptr || offset == nullptr) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_ipc_export: null pointer");
+  }
+  using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static AddressRangeFn range_fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      range_fn = reinterpret_cast<AddressRangeFn>(f);
+    }
+  });
+  if (range_fn == nullptr) return fail(ARC_ERR_CUDA, "cuMemGetAddressRange is unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range_fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_ipc_export: %p is not device memory", ptr);
+  }
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<uint64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return ARC_OK;
+}
+
+int arc_ipc_open(const void* handle, uint64_t offset, void** ptr, void** base) {
+  g_last_error[0] = '\0';
+  if (handle == nullptr || ptr == nullptr || base == nullptr) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_ipc_open: null pointer");
+  }
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* b = nullptr;
+  // Opened in the current device's context: its kernels are the ones that access the
+  // mapping, and the flag enables peer access from it to the owner's GPU.
+  const cudaError_t e = cudaIpcOpenMemHandle(&b, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  *base = b;
+  *ptr = static_cast<uint8_t*>(b) + offset;
+  return ARC_OK;
+}
+
+int arc_ipc_close(void* base) {
+  g_last_error[0] = '\0';
+  if (base == nullptr) return fail(ARC_ERR_INVALID_ARGUMENT, "arc_ipc_close: null pointer");
+  const cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+  return ARC_OK;
+}
+
 int arc_peer_barrier(uint32_t* const* flags, int world, int rank, uint32_t epoch, cudaStream_t stream) {
   g_last_error[0] = '\0';
   if (flags == nullptr || world < 1 || world > static_cast<int>(arcb::peer::kMaxPeers) || rank < 0 ||

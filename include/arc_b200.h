@@ -146,6 +146,21 @@ int arc_a8w4_gemm_gather(const int8_t *A, const float *sa, const uint8_t *Wp, co
 int arc_peer_barrier(uint32_t *const *flags, int world, int rank, uint32_t epoch, cudaStream_t stream);
 
 /*
+ * CUDA IPC for the buffers of a fused all-gather (no reference counterpart: the reference
+ * is single-GPU). arc_ipc_export writes the ARC_IPC_HANDLE_BYTES-byte handle of the
+ * device allocation that holds `ptr` and ptr's byte offset inside it. arc_ipc_open maps a
+ * handle exported by ANOTHER process into the CURRENT device's context (make the GPU
+ * whose kernels will access the buffer current first), enabling peer access from it to
+ * the owner's GPU; *ptr = mapping + offset, *base is what arc_ipc_close takes. A process
+ * opens each handle once; the owner frees the allocation only after every importer
+ * closed it.
+ */
+#define ARC_IPC_HANDLE_BYTES 64
+int arc_ipc_export(const void *ptr, void *handle, uint64_t *offset);
+int arc_ipc_open(const void *handle, uint64_t offset, void **ptr, void **base);
+int arc_ipc_close(void *base);
+
+/*
  * FP8 x FP4 GEMM with UE8M0 block scales, the recipe of the reference's A8W4 test
  * (tests/a8w4.py:29-30 quantisation, :48 the deep_gemm.fp8_fp4_gemm_nt call with
  * recipe_a = (1, 128), recipe_b = (1, 32)):

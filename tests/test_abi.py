@@ -81,6 +81,12 @@ def test_invalid_arguments_are_rejected_before_any_cuda_call(native_lib):
         _lib.ARC_ERR_INVALID_ARGUMENT
     assert L.arc_a8w4_gemm_gather(p, p, p, p, outs, 2, 0, 64, 64, 256, nul) == _lib.ARC_ERR_UNSUPPORTED
     assert L.arc_peer_barrier(outs, 2, 2, 1, nul) == _lib.ARC_ERR_INVALID_ARGUMENT
+    # CUDA IPC helpers: missing handle / output arguments
+    off = ctypes.c_uint64()
+    vp, vb = ctypes.c_void_p(), ctypes.c_void_p()
+    assert L.arc_ipc_export(nul, p, ctypes.byref(off)) == _lib.ARC_ERR_INVALID_ARGUMENT
+    assert L.arc_ipc_open(nul, 0, ctypes.byref(vp), ctypes.byref(vb)) == _lib.ARC_ERR_INVALID_ARGUMENT
+    assert L.arc_ipc_close(nul) == _lib.ARC_ERR_INVALID_ARGUMENT
     # kernel-name query: no buffer / non-positive sizes
     assert L.arc_kernel_name(0, 8, 8, 8, nul, 16) == _lib.ARC_ERR_INVALID_ARGUMENT
     assert L.arc_kernel_name(0, 0, 8, 8, ctypes.cast(buf, ctypes.c_char_p), 16) == \

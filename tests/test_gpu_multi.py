@@ -107,9 +107,8 @@ def _fused_worker(rank, world, port, m, n, k, result_q):
             torch.cuda.synchronize()
             ok = ok and bool(torch.equal(got, ref)) and arc.device_status(rank) == 0
             dist.barrier()
+        fg.close()
         result_q.put((rank, ok))
-        dist.barrier()
-        del fg
     finally:
         dist.destroy_process_group()
 
@@ -126,7 +125,7 @@ def test_two_gpu_fused_all_gather(m, n, k):
     for p in procs:
         p.start()
     try:
-        results = dict(q.get(timeout=240) for _ in range(world))
+        results = dict(q.get(timeout=180) for _ in range(world))
     finally:
         for p in procs:
             p.join(timeout=120)
