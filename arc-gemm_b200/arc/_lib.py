@@ -61,7 +61,7 @@ SIGNATURES = {
     "arc_fp8_fp4_workspace_bytes": ([_I, _I, _I, ctypes.POINTER(ctypes.c_size_t)], _I),
     "arc_fp8_fp4_gemm_noalloc": ([_P, _P, _P, _P, _P, _I, _I, _I, _P], _I),
     "arc_a8w4_gemm_gather": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
-    "arc_peer_barrier": ([_P, _I, _I, ctypes.c_uint32, _P], _I),
+    "arc_peer_barrier": ([_P, _I, _I, _P], _I),
     "arc_ipc_export": ([_P, _P, ctypes.POINTER(ctypes.c_uint64)], _I),
     "arc_ipc_open": ([_P, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)], _I),
     "arc_ipc_close": ([_P], _I),

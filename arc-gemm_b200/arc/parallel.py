@@ -130,7 +130,8 @@ class FusedGather:
         out_bytes = -(-m * n_total * 2 // 256) * 256
         self._buf = torch.zeros(out_bytes + 256, dtype=torch.uint8, device=self.device)
         self.out = self._buf[: m * n_total * 2].view(torch.bfloat16).view(m, n_total)
-        self.flags = self._buf[out_bytes: out_bytes + 4 * self.world].view(torch.int32)
+        # world epoch flags, then this rank's barrier counter
+        self.flags = self._buf[out_bytes: out_bytes + 4 * (self.world + 1)].view(torch.int32)
         torch.cuda.synchronize(self.device)
         handle = ctypes.create_string_buffer(64)
         offset = ctypes.c_uint64()
@@ -152,7 +153,6 @@ class FusedGather:
                 flags.append(base + out_bytes)
         self._outs = (ctypes.c_void_p * self.world)(*outs)
         self._flags = (ctypes.c_void_p * self.world)(*flags)
-        self.epoch = 0
         dist.barrier(group=group)  # every mapping exists before any rank writes into it
 
     def matmul(self, a: TensorPair, b_local: TensorPair) -> torch.Tensor:
@@ -175,9 +175,7 @@ class FusedGather:
             check(lib().arc_a8w4_gemm_gather(x.data_ptr(), sa.data_ptr(), wp.data_ptr(), sb.data_ptr(),
                                              self._outs, self.world, self.rank, m, n, k, stream),
                   "arc_a8w4_gemm_gather")
-            self.epoch += 1
-            check(lib().arc_peer_barrier(self._flags, self.world, self.rank, self.epoch, stream),
-                  "arc_peer_barrier")
+            check(lib().arc_peer_barrier(self._flags, self.world, self.rank, stream), "arc_peer_barrier")
         return self.out
 
     def close(self) -> None:

@@ -852,7 +852,7 @@ int arc_ipc_close(void* base) {
   return ARC_OK;
 }
 
-int arc_peer_barrier(uint32_t* const* flags, int world, int rank, uint32_t epoch, cudaStream_t stream) {
+int arc_peer_barrier(uint32_t* const* flags, int world, int rank, cudaStream_t stream) {
   g_last_error[0] = '\0';
   if (flags == nullptr || world < 1 || world > static_cast<int>(arcb::peer::kMaxPeers) || rank < 0 ||
       rank >= world) {
@@ -867,7 +867,6 @@ int arc_peer_barrier(uint32_t* const* flags, int world, int rank, uint32_t epoch
   }
   b.world = static_cast<uint32_t>(world);
   b.rank = static_cast<uint32_t>(rank);
-  b.epoch = epoch;
   int dev = 0;
   if (int st = current_device(&dev)) return st;
   arcb::peer::peer_barrier_kernel<<<1, 32, 0, stream>>>(b);

@@ -386,7 +386,9 @@ def run_ours(args, wl, world, rank, local):
 
         def call(s):
             return fused.matmul(s[0], s[1])
-    use_graph = flush is None and not args.no_graph and not gather
+    # The fused gather's barrier keeps its epoch on the device, so its steps capture into
+    # a graph like the GEMM alone; the NCCL gather runs eagerly.
+    use_graph = flush is None and not args.no_graph and gather != "nccl"
     stream = torch.cuda.Stream(device)
     peaks = load_peaks()
 
@@ -407,8 +409,12 @@ def run_ours(args, wl, world, rank, local):
             # collective in the step every rank must run the same number of steps, so
             # that case settles for a fixed count instead of a wall-clock time.
             if gather:
-                for i in range(int(args.settle_s * 2000)):
-                    call(sets[i % n_sets])
+                if graph is not None:
+                    for _ in range(max(1, int(args.settle_s * 2000) // args.steps)):
+                        graph.replay()
+                else:
+                    for i in range(int(args.settle_s * 2000)):
+                        call(sets[i % n_sets])
                 torch.cuda.synchronize()
             t_end = time.time() + (0.0 if gather else args.settle_s)
             while time.time() < t_end:
@@ -451,6 +457,8 @@ def run_ours(args, wl, world, rank, local):
 
             # e2e through the public API with pinned host buffers (untimed warm-up first).
             e2e = run_e2e(args, wl, sets[0], device, stream, world)
+            if gather == "fused":
+                fused.close()
 
     clk = clocks.summary()
     step_ms = max_over_ranks(elapsed_ms / args.steps, world)
@@ -495,7 +503,8 @@ def run_ours(args, wl, world, rank, local):
                        l2=("rotating %d distinct input sets (%.0f MB) > L2" %
                            (n_sets, n_sets * in_bytes / 1e6)) if flush is None
                        else "L2 flushed (512 MB write) before every timed step",
-                       launch="K launches in one CUDA graph" if use_graph else "eager launches",
+                       launch=(f"K steps ({launches_per_step} launch(es) each) in one CUDA graph"
+                               if use_graph else "eager launches"),
                        allgather={"nccl": "NCCL all_gather_into_tensor of the bf16 output every step",
                                   "fused": "fused into the GEMM epilogue: TMA stores of every tile "
                                            "into each rank's output over NVLink + a flag barrier"

@@ -137,13 +137,16 @@ int arc_a8w4_gemm_gather(const int8_t *A, const float *sa, const uint8_t *Wp, co
                          cudaStream_t stream);
 
 /*
- * Stream-ordered barrier of the ranks of a fused all-gather: announces `epoch` in every
- * rank's flag array (flags[i]: rank i's `world` uint32 flags, zeroed once, mapped into
- * this process) and waits on `stream` until this rank's array holds an epoch >= `epoch`
- * from every rank. Epochs must grow by one per call, in the same order on every rank.
- * The wait gives up after 2 s and reports it through arc_device_status.
+ * Stream-ordered barrier of the ranks of a fused all-gather. flags[i] is rank i's array
+ * of world + 1 uint32 words, zeroed once and mapped into this process: words 0..world-1
+ * hold the last epoch each rank announced, word `world` counts the barriers rank i has
+ * passed. The call takes this rank's next epoch from its counter, announces it in every
+ * rank's array and waits on `stream` until this rank's array holds that epoch from every
+ * rank. Every rank must call it the same number of times. The epoch is kept in device
+ * memory, so a CUDA graph that captured the call replays correctly. The wait gives up
+ * after 2 s and reports it through arc_device_status.
  */
-int arc_peer_barrier(uint32_t *const *flags, int world, int rank, uint32_t epoch, cudaStream_t stream);
+int arc_peer_barrier(uint32_t *const *flags, int world, int rank, cudaStream_t stream);
 
 /*
  * CUDA IPC for the buffers of a fused all-gather (no reference counterpart: the reference

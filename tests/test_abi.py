@@ -80,7 +80,7 @@ def test_invalid_arguments_are_rejected_before_any_cuda_call(native_lib):
     assert L.arc_a8w4_gemm_gather(p, p, p, p, outs, 9, 0, 16, 64, 256, nul) == \
         _lib.ARC_ERR_INVALID_ARGUMENT
     assert L.arc_a8w4_gemm_gather(p, p, p, p, outs, 2, 0, 64, 64, 256, nul) == _lib.ARC_ERR_UNSUPPORTED
-    assert L.arc_peer_barrier(outs, 2, 2, 1, nul) == _lib.ARC_ERR_INVALID_ARGUMENT
+    assert L.arc_peer_barrier(outs, 2, 2, nul) == _lib.ARC_ERR_INVALID_ARGUMENT
     # CUDA IPC helpers: missing handle / output arguments
     off = ctypes.c_uint64()
     vp, vb = ctypes.c_void_p(), ctypes.c_void_p()

@@ -107,6 +107,24 @@ def _fused_worker(rank, world, port, m, n, k, result_q):
             torch.cuda.synchronize()
             ok = ok and bool(torch.equal(got, ref)) and arc.device_status(rank) == 0
             dist.barrier()
+        # The same call captured once in a CUDA graph and replayed on new inputs: the
+        # barrier's epoch lives on the device, so every replay synchronises afresh.
+        (x, sa), (wp, sb) = generate_a8w4(m, n, k, seed=7)
+        xs, sas, wps, sbs = x.to(dev), sa.to(dev), wp.to(dev), sb.to(dev)
+        b_static = par.shard_weights((wps, sbs), rank, world)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fg.matmul((xs, sas), b_static)
+        for seed in (8, 9):
+            (x, sa), (wp, sb) = generate_a8w4(m, n, k, seed=seed)
+            for dst, src in ((xs, x), (sas, sa), (wps, wp), (sbs, sb)):
+                dst.copy_(src)
+            ref = par.sharded_gemm(arc.a8w4_matmul, (xs, sas), b_static, world=world, all_gather=True)
+            graph.replay()
+            torch.cuda.synchronize()
+            ok = ok and bool(torch.equal(fg.out, ref)) and arc.device_status(rank) == 0
+            dist.barrier()
+        del graph
         fg.close()
         result_q.put((rank, ok))
     finally:
