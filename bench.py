@@ -343,16 +343,26 @@ def run_ours(args, wl, world, rank, local):
     if args.prepacked:
         if wl["kind"] != "a8w4":
             raise SystemExit("--prepacked applies to the A8W4 workloads")
-        # One-time weight format step, outside the timed region; its own kernel time is
-        # reported beside the line (in place, one call per input set, HBM-bound).
-        arc.prepack_weights(sets[0][1][0])  # untimed first call (library and module setup)
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in sets]
-        for st, (e0, e1) in zip(sets, evs):
-            e0.record()
-            arc.prepack_weights(st[1][0], out=st[1][0])
-            e1.record()
+        # One-time weight format step, outside the timed region. Its own kernel time is
+        # reported beside the line: out-of-place calls over every set's weights into one
+        # scratch buffer, enqueued back to back behind a GPU sleep so that the events
+        # bracket device work only (HBM-bound; the sets' weights exceed L2).
+        scratch = torch.empty_like(sets[0][1][0])
+        arc.prepack_weights(sets[0][1][0], out=scratch)  # untimed first call (library setup)
         torch.cuda.synchronize(device)
-        pp_us = sum(e0.elapsed_time(e1) for e0, e1 in evs) * 1e3 / len(sets)
+        pp0 = torch.cuda.Event(enable_timing=True)
+        pp1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(5_000_000)  # ~2.5 ms: the host enqueues every call meanwhile
+        pp0.record()
+        for st in sets:
+            arc.prepack_weights(st[1][0], out=scratch)
+        pp1.record()
+        torch.cuda.synchronize(device)
+        pp_us = pp0.elapsed_time(pp1) * 1e3 / len(sets)
+        del scratch
+        for st in sets:
+            arc.prepack_weights(st[1][0], out=st[1][0])
+        torch.cuda.synchronize(device)
         pp_bytes = 2 * N * K // 2  # every packed byte read once and written once
         prepack_info = {"us_per_call": pp_us, "bytes_per_call": pp_bytes,
                         "gbs": pp_bytes / (pp_us * 1e-6) / 1e9, "calls": len(sets)}
