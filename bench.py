@@ -466,7 +466,9 @@ def run_ours(args, wl, world, rank, local):
             del graph
 
             # e2e through the public API with pinned host buffers (untimed warm-up first).
-            e2e = run_e2e(args, wl, sets[0], device, stream, world)
+            e2e = run_e2e(args, wl, sets[0], device, stream, world,
+                          gemm=(fused.matmul if gather == "fused" else None),
+                          gather_nccl=(gather == "nccl"))
             if gather == "fused":
                 fused.close()
 
@@ -545,8 +547,13 @@ def run_ours(args, wl, world, rank, local):
     print(json.dumps(line))
 
 
-def run_e2e(args, wl, s, device, stream, world):
-    """Host buffers in, host buffer out, through the public API, K steps."""
+def run_e2e(args, wl, s, device, stream, world, gemm=None, gather_nccl=False):
+    """Host buffers in, host buffer out, through the public API, K steps.
+
+    gemm: the A8W4 call to time instead of arc.a8w4_matmul (FusedGather.matmul, whose
+    output is the gathered [M, world*N]); gather_nccl: follow the GEMM with the NCCL
+    all-gather of its output, as the timed step does.
+    """
     import torch
 
     import arc
@@ -555,15 +562,26 @@ def run_e2e(args, wl, s, device, stream, world):
         (x, sa), (wp, sb), _ = s
         host = [t.cpu().pin_memory() for t in (x, sa, wp, sb)]
         dev_bufs = [torch.empty_like(t) for t in (x, sa, wp, sb)]
-        out_h = torch.empty((wl["M"], wl["N"]), dtype=torch.bfloat16).pin_memory()
+        n_out = wl["N"] * world if gemm is not None else wl["N"]
+        m_out = wl["M"] * world if gather_nccl else wl["M"]
+        out_h = torch.empty((m_out, n_out), dtype=torch.bfloat16).pin_memory()
         out_d = torch.empty((wl["M"], wl["N"]), dtype=torch.bfloat16, device=device)
+        if gather_nccl:
+            import torch.distributed as dist
+
+            gathered = torch.empty((m_out, n_out), dtype=torch.bfloat16, device=device)
 
         def step():
             for h, d in zip(host, dev_bufs):
                 d.copy_(h, non_blocking=True)
-            if wl["kind"] == "a8w4":
+            if gemm is not None:
+                o = gemm((dev_bufs[0], dev_bufs[1]), (dev_bufs[2], dev_bufs[3]))
+            elif wl["kind"] == "a8w4":
                 o = arc.a8w4_matmul((dev_bufs[0], dev_bufs[1]), (dev_bufs[2], dev_bufs[3]),
                                     prepacked=args.prepacked)
+                if gather_nccl:
+                    dist.all_gather_into_tensor(gathered, o)
+                    o = gathered
             else:
                 o = arc.fp8_fp4_gemm_nt((dev_bufs[0], dev_bufs[1]), (dev_bufs[2], dev_bufs[3]), out_d)
             out_h.copy_(o, non_blocking=True)
