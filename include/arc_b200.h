@@ -11,7 +11,9 @@
  *
  * Conventions shared by every entry point:
  *   - All pointers are device pointers of the current CUDA device; the caller owns
- *     every buffer (the reference allocates `out` in Python, arc/mm.py:76-77).
+ *     every buffer (the reference allocates `out` in Python, arc/mm.py:76-77). The
+ *     fused all-gather calls are the exception: they also take other GPUs' buffers,
+ *     mapped into this process with arc_ipc_open.
  *   - Work is enqueued on `stream` and the call returns without synchronising, as the
  *     reference launches on the caller's stream (arc/mm.py:38,44).
  *   - The return value is an arc_status_t. Where the reference would exit() the
@@ -22,7 +24,8 @@
  *   - Kernels never wait without a bound: a pipeline wait that exceeds 2 s records a
  *     bit in a per-device status word (read with arc_device_status()) and the kernel
  *     returns.
- *   - Nothing here allocates device memory.
+ *   - Nothing here allocates device memory (arc_ipc_open maps a peer's existing
+ *     allocation; it allocates none).
  */
 #ifndef ARC_B200_H_
 #define ARC_B200_H_
