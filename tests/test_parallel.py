@@ -90,3 +90,36 @@ def test_sharded_a8w4_all_gather_two_ranks():
         assert np.array_equal(full, single)
         lo, hi = parallel.column_range(64, r, world)
         assert np.array_equal(local, single[:, lo:hi])
+
+
+def test_ipc_mappings_open_once_per_handle(monkeypatch):
+    """FusedGather's peer mappings: a process opens each exported allocation once (CUDA
+    allows one mapping per handle and process), shares it between users at their own
+    offsets, and closes it when the last user goes. The library is a fake here."""
+    from arc import _lib
+
+    calls = []
+
+    class FakeLib:
+        def arc_ipc_open(self, handle, offset, ptr, base):
+            calls.append(("open", bytes(handle), offset))
+            ptr._obj.value = 0x10000 + offset
+            base._obj.value = 0x10000
+            return 0
+
+        def arc_ipc_close(self, base):
+            calls.append(("close", base))
+            return 0
+
+    monkeypatch.setattr(_lib, "lib", lambda: FakeLib())
+    monkeypatch.setattr(parallel, "_OPENED", {})
+    h = bytes(range(64))
+    p1, k1 = parallel._ipc_open(h, 256)
+    p2, k2 = parallel._ipc_open(h, 4096)
+    assert (p1, p2) == (0x10000 + 256, 0x10000 + 4096)
+    assert calls == [("open", h, 0)]
+    parallel._ipc_close(k1)
+    assert len(calls) == 1
+    parallel._ipc_close(k2)
+    assert calls[-1] == ("close", 0x10000)
+    assert parallel._OPENED == {}
