@@ -145,7 +145,7 @@ def _check_on_device(out: torch.Tensor, ref: torch.Tensor, max_ulp: float = 2.0)
     assert n_bad == 0, f"{n_bad} of {ref.numel()} elements beyond {max_ulp} ulp + {atol:.3g}"
 
 
-@pytest.mark.parametrize("m", [1, 16, 128, 1024])
+@pytest.mark.parametrize("m", [1, 16, 128, 1024, 8192])
 def test_a8w4_large_weight_sweep(cuda_device, m):
     """N=28672, K=8192 at the sweep's token counts."""
     n, k = 28672, 8192
