@@ -67,7 +67,13 @@ SIGNATURES = {
     "arc_ipc_close": ([_P], _I),
     "arc_a8w4_prepack_weights": ([_P, _P, _I, _I, _P], _I),
     "arc_a8w4_gemm_prepacked": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _P], _I),
+    "arc_a8w4_gemm_ex": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_uint, _P, _P], _I),
+    "arc_a8w4_gemm_gather_ex": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, ctypes.c_uint, _P], _I),
 }
+
+# Flags of arc_a8w4_gemm_ex / arc_a8w4_gemm_gather_ex (include/arc_b200.h).
+A8W4_PREPACKED = 1
+A8W4_STATIC_WEIGHTS = 2
 
 # Operation codes of arc_kernel_name (include/arc_b200.h).
 OP_MATMUL_BF16, OP_A8W4, OP_FP8_FP4 = 0, 1, 2

@@ -14,7 +14,7 @@ int8 x int4 recipe:
     out[m, n] = bf16( sa[m] * sum_g f32(sb[n, g]) * P[m, n, g] ),
     P[m, n, g] = sum_{k in group g} x[m, k] * w[n, k]   (int32, exact)
 
-Everything runs in `arc_a8w4_gemm` (include/arc_b200.h) on the caller's stream.
+Everything runs in `arc_a8w4_gemm_ex` (include/arc_b200.h) on the caller's stream.
 """
 from __future__ import annotations
 
@@ -23,7 +23,7 @@ from typing import Sequence
 
 import torch
 
-from ._lib import check, lib
+from ._lib import A8W4_PREPACKED, A8W4_STATIC_WEIGHTS, check, lib
 from .quant import TensorPair
 
 GROUP_K = 128
@@ -50,13 +50,18 @@ def _expect(t: torch.Tensor, name: str, dtype: torch.dtype, shape: tuple, device
 
 def a8w4_matmul(a: TensorPair, b: TensorPair, out: torch.Tensor | None = None, *,
                 group: int = GROUP_K, partials: torch.Tensor | None = None,
-                prepacked: bool = False) -> torch.Tensor:
+                prepacked: bool = False, static_weights: bool = False) -> torch.Tensor:
     """out = A8W4 GEMM of (x, sa) and (wp, sb). See the module docstring.
 
     `partials`, if given, is an int32 [M, N, K/128] tensor that receives every exact
     group partial P[m, n, g] (a slow debugging mode).
     `prepacked=True` says wp is in the pre-packed layout of `prepack_weights` (same
     shape; results identical to the original packing).
+    `static_weights=True` promises that wp and sb are not written by the kernel that
+    directly precedes this call on the current stream (true of model weights loaded
+    once). Decode-sized calls (M <= 32) then stream and unpack the weights while that
+    kernel is still running, so back-to-back GEMMs overlap their weight traffic.
+    Results are the same either way.
     """
     x, sa = a
     wp, sb = b
@@ -77,21 +82,16 @@ def a8w4_matmul(a: TensorPair, b: TensorPair, out: torch.Tensor | None = None, *
         out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
     else:
         _expect(out, "out", torch.bfloat16, (m, n), dev)
+    if prepacked and partials is not None:
+        raise ValueError("partials are not available with prepacked weights")
     pptr = None
-    if prepacked:
-        if partials is not None:
-            raise ValueError("partials are not available with prepacked weights")
-        with torch.cuda.device(dev):
-            check(lib().arc_a8w4_gemm_prepacked(x.data_ptr(), sa.data_ptr(), wp.data_ptr(), sb.data_ptr(),
-                                                out.data_ptr(), m, n, k, group, _stream_ptr(dev)),
-                  "arc.a8w4_matmul")
-        return out
     if partials is not None:
         _expect(partials, "partials", torch.int32, (m, n, k // group), dev)
         pptr = partials.data_ptr()
+    flags = (A8W4_PREPACKED if prepacked else 0) | (A8W4_STATIC_WEIGHTS if static_weights else 0)
     with torch.cuda.device(dev):
-        check(lib().arc_a8w4_gemm(x.data_ptr(), sa.data_ptr(), wp.data_ptr(), sb.data_ptr(),
-                                  out.data_ptr(), m, n, k, group, _stream_ptr(dev), pptr),
+        check(lib().arc_a8w4_gemm_ex(x.data_ptr(), sa.data_ptr(), wp.data_ptr(), sb.data_ptr(),
+                                     out.data_ptr(), m, n, k, group, flags, _stream_ptr(dev), pptr),
               "arc.a8w4_matmul")
     return out
 

@@ -155,10 +155,11 @@ class FusedGather:
         self._flags = (ctypes.c_void_p * self.world)(*flags)
         dist.barrier(group=group)  # every mapping exists before any rank writes into it
 
-    def matmul(self, a: TensorPair, b_local: TensorPair) -> torch.Tensor:
+    def matmul(self, a: TensorPair, b_local: TensorPair, static_weights: bool = False) -> torch.Tensor:
         """This rank's column block of the A8W4 decode GEMM, stored into every rank's
-        output, then the barrier after which `out` holds all blocks."""
-        from ._lib import check, lib
+        output, then the barrier after which `out` holds all blocks.
+        `static_weights` as in `arc.a8w4_matmul`."""
+        from ._lib import A8W4_STATIC_WEIGHTS, check, lib
 
         x, sa = a
         wp, sb = b_local
@@ -172,8 +173,9 @@ class FusedGather:
                 raise ValueError(f"operand on {t.device}, expected {self.device}")
         stream = torch.cuda.current_stream(self.device).cuda_stream
         with torch.cuda.device(self.device):
-            check(lib().arc_a8w4_gemm_gather(x.data_ptr(), sa.data_ptr(), wp.data_ptr(), sb.data_ptr(),
-                                             self._outs, self.world, self.rank, m, n, k, stream),
+            check(lib().arc_a8w4_gemm_gather_ex(x.data_ptr(), sa.data_ptr(), wp.data_ptr(), sb.data_ptr(),
+                                                self._outs, self.world, self.rank, m, n, k,
+                                                A8W4_STATIC_WEIGHTS if static_weights else 0, stream),
                   "arc_a8w4_gemm_gather")
             check(lib().arc_peer_barrier(self._flags, self.world, self.rank, stream), "arc_peer_barrier")
         return self.out

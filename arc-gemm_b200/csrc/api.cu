@@ -328,85 +328,45 @@ uint32_t ceil_div(uint32_t a, uint32_t b) { return (a + b - 1) / b; }
 // ---------------------------------------------------------------------------------
 constexpr uint32_t kDecodeMaxM = 32;
 
-uint32_t decode_stage_bytes(uint32_t bt, uint32_t R, uint32_t gps) {
-  return ceil_div(gps * (bt * arcb::a8w4::kGroupK + R * arcb::a8w4::kPackedRow), 1024) * 1024;
-}
-
-// Groups per ring stage: the largest of 8, 4, 2 for which two stages fit the ring.
-uint32_t decode_gps(uint32_t bt, uint32_t R) {
-  for (uint32_t gps = 8; gps > 2; gps /= 2) {
-    if (arcb::a8w4dec::kRingBytes / decode_stage_bytes(bt, R, gps) >= 2) return gps;
-  }
-  return 2;
-}
-
-uint32_t decode_stages(uint32_t bt, uint32_t R, uint32_t gps) {
-  const uint32_t n = arcb::a8w4dec::kRingBytes / decode_stage_bytes(bt, R, gps);
-  return n < arcb::a8w4dec::kMaxStages ? n : arcb::a8w4dec::kMaxStages;
-}
-
-// Decode-sized problems (M <= 32) stream the weights once. A plan is a tile height R
-// (multiple of 8 in [32, 128]) and a K split S in {1, 2, 4} (S > 1: one wave of
-// S-CTA clusters reducing on chip; S == 1: persistent unsplit tiles). Its estimated
-// time is the largest of
-//   * issuing the CTA's tcgen05.mma instructions (4 per K-group, ~55 cycles each
-//     whatever R is: so tall tiles and K splits pay off),
-//   * streaming the whole weight matrix at HBM speed,
-//   * streaming one CTA's share through one SM,
-// plus a fixed cost for the cluster exchange when S > 1.
+// Decode-sized problems (M <= 32) stream the weights once, in 128-row tiles. A plan is a
+// K split S in {1, 2, 4}: S > 1 runs one wave of S-CTA clusters that reduce on chip
+// (every CTA streams 1/S of a tile's K-groups); S == 1 runs persistent CTAs over whole
+// tiles. The largest S whose grid stays within one CTA per SM is taken, so that the next
+// launch in the stream finds a free slot on every SM (two decode CTAs fit on one SM) and
+// overlaps this one; each CTA's UMMA issue (four per K-group) shrinks with S.
 //
-// ARC_DECODE_PLAN="R:S[:GPS]" (tuning and tests only) forces a decode decomposition
-// (and optionally the K-groups per ring stage); it is ignored unless it is valid for
-// the shape and device.
-bool decode_override(uint32_t N, uint32_t G, int sms, int max_c2, int max_c4, uint32_t bt,
-                     arc_a8w4_plan_t* plan);
+// ARC_DECODE_PLAN="128:S[:grid]" (tuning and tests only) forces the K split, and for
+// S == 1 optionally caps the grid (so that CTAs walk several tiles); it is ignored unless
+// it is valid for the shape and device.
+bool decode_override(uint32_t tiles, uint32_t G, int sms, int max_c2, int max_c4, arc_a8w4_plan_t* plan);
+
+void decode_plan(uint32_t bt, uint32_t S, uint32_t grid, arc_a8w4_plan_t* plan) {
+  plan->split = S > 1 ? 1 : 0;
+  plan->token_tile = static_cast<int>(bt);
+  plan->weight_rows = static_cast<int>(arcb::a8w4::kRows);
+  plan->k_split = static_cast<int>(S);
+  plan->grid = static_cast<int>(grid);
+  plan->load_stages = static_cast<int>(arcb::a8w4dec::kWStages);
+  plan->groups_per_stage = static_cast<int>(arcb::a8w4dec::kGps);
+}
 
 int plan_a8w4(int M, int N, int K, int sms, int max_c2, int max_c4, arc_a8w4_plan_t* plan) {
   const uint32_t G = static_cast<uint32_t>(K) / arcb::a8w4::kGroupK;
   if (M <= static_cast<int>(kDecodeMaxM)) {
     const uint32_t bt = M <= 16 ? 16u : 32u;
-    if (decode_override(N, G, sms, max_c2, max_c4, bt, plan)) return ARC_OK;
-    constexpr double kGroupIssueNs = 4.0 * 55.0 / 1.9;
-    constexpr double kHbmBytesPerNs = 6500.0;
-    constexpr double kSmBytesPerNs = 120.0;
-    constexpr double kClusterNs = 500.0;
-    const double total_bytes = static_cast<double>(N) * K / 2;
-    double best = 1e300;
-    arc_a8w4_plan_t bp{};
-    for (uint32_t S = 1; S <= 4; S *= 2) {
-      if (S > G) continue;
-      const int cap = S == 1 ? 1 << 30 : (S == 2 ? max_c2 : max_c4);
-      for (uint32_t R = 128; R >= 32; R -= 8) {
-        if ((R / S) % 8 || R % S) continue;  // output columns per CTA: 16-byte TMA rows
-        const uint32_t tiles = ceil_div(static_cast<uint32_t>(N), R);
-        uint32_t groups, grid;
-        if (S > 1) {
-          if (tiles > static_cast<uint32_t>(cap)) continue;  // must be one wave
-          groups = ceil_div(G, S);
-          grid = tiles * S;
-        } else {
-          groups = G * ceil_div(tiles, static_cast<uint32_t>(sms));
-          grid = tiles < static_cast<uint32_t>(sms) ? tiles : static_cast<uint32_t>(sms);
-        }
-        const double t_issue = groups * kGroupIssueNs;
-        const double t_sm = static_cast<double>(R) * groups * arcb::a8w4::kPackedRow / kSmBytesPerNs;
-        double t = t_issue > t_sm ? t_issue : t_sm;
-        if (total_bytes / kHbmBytesPerNs > t) t = total_bytes / kHbmBytesPerNs;
-        if (S > 1) t += kClusterNs;
-        if (t < best - 1e-6) {
-          best = t;
-          const uint32_t gps = decode_gps(bt, R);
-          bp.split = S > 1 ? 1 : 0;
-          bp.token_tile = static_cast<int>(bt);
-          bp.weight_rows = static_cast<int>(R);
-          bp.k_split = static_cast<int>(S);
-          bp.grid = static_cast<int>(grid);
-          bp.load_stages = static_cast<int>(decode_stages(bt, R, gps));
-          bp.groups_per_stage = static_cast<int>(gps);
-        }
+    const uint32_t tiles = ceil_div(static_cast<uint32_t>(N), arcb::a8w4::kRows);
+    if (decode_override(tiles, G, sms, max_c2, max_c4, plan)) {
+      plan->token_tile = static_cast<int>(bt);
+      return ARC_OK;
+    }
+    for (uint32_t S : {4u, 2u}) {
+      const int cap = S == 2 ? max_c2 : max_c4;
+      if (S <= G && tiles * S <= static_cast<uint32_t>(sms) && tiles <= static_cast<uint32_t>(cap)) {
+        decode_plan(bt, S, tiles * S, plan);
+        return ARC_OK;
       }
     }
-    *plan = bp;
+    decode_plan(bt, 1, tiles < static_cast<uint32_t>(sms) ? tiles : static_cast<uint32_t>(sms), plan);
     return ARC_OK;
   }
   const uint32_t bt = M <= 64 ? 64u : 128u;
@@ -422,30 +382,15 @@ int plan_a8w4(int M, int N, int K, int sms, int max_c2, int max_c4, arc_a8w4_pla
   return ARC_OK;
 }
 
-bool decode_override(uint32_t N, uint32_t G, int sms, int max_c2, int max_c4, uint32_t bt,
-                     arc_a8w4_plan_t* plan) {
+bool decode_override(uint32_t tiles, uint32_t G, int sms, int max_c2, int max_c4, arc_a8w4_plan_t* plan) {
   const char* env = getenv("ARC_DECODE_PLAN");
-  unsigned R = 0, S = 0, gps_req = 0;
-  if (env == nullptr || sscanf(env, "%u:%u:%u", &R, &S, &gps_req) < 2) return false;
-  if (R < 32 || R > 128 || R % 8 || !(S == 1 || S == 2 || S == 4) || S > G || R % S ||
-      (R / S) % 8) {
-    return false;
-  }
-  const uint32_t tiles = ceil_div(N, R);
+  unsigned R = 0, S = 0, grid_cap = 0;
+  if (env == nullptr || sscanf(env, "%u:%u:%u", &R, &S, &grid_cap) < 2) return false;
+  if (R != arcb::a8w4::kRows || !(S == 1 || S == 2 || S == 4) || S > G) return false;
   if (S > 1 && tiles > static_cast<uint32_t>(S == 2 ? max_c2 : max_c4)) return false;
-  uint32_t gps = decode_gps(bt, R);
-  if (gps_req == 2 || gps_req == 4 || gps_req == 8) {
-    if (arcb::a8w4dec::kRingBytes / decode_stage_bytes(bt, R, gps_req) < 2) return false;
-    gps = gps_req;
-  }
-  if (arcb::a8w4dec::kSlotBytes / (R * arcb::a8w4::kGroupK) < gps) return false;
-  plan->split = S > 1 ? 1 : 0;
-  plan->token_tile = static_cast<int>(bt);
-  plan->weight_rows = static_cast<int>(R);
-  plan->k_split = static_cast<int>(S);
-  plan->grid = static_cast<int>(S > 1 ? tiles * S : (tiles < static_cast<uint32_t>(sms) ? tiles : sms));
-  plan->load_stages = static_cast<int>(decode_stages(bt, R, gps));
-  plan->groups_per_stage = static_cast<int>(gps);
+  uint32_t grid = S > 1 ? tiles * S : (tiles < static_cast<uint32_t>(sms) ? tiles : static_cast<uint32_t>(sms));
+  if (S == 1 && grid_cap > 0 && grid_cap < grid) grid = grid_cap;
+  decode_plan(16, S, grid, plan);
   return true;
 }
 
@@ -569,7 +514,7 @@ int fp8fp4_gemm(const uint8_t* A, const float* sfa, const uint8_t* Wp, const flo
                 int M, int N, int K, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 int a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_t* sb, uint16_t* C, int M,
               int N, int K, int group, cudaStream_t stream, int32_t* partials_dbg, uint16_t* const* outs,
-              int world, int rank, uint32_t split);
+              int world, int rank, uint32_t flags);
 
 }  // namespace
 
@@ -730,10 +675,22 @@ int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uin
   return a8w4_gemm(A, sa, Wp, sb, C, M, N, K, group, stream, partials_dbg, nullptr, 0, 0, 0u);
 }
 
+int arc_a8w4_gemm_ex(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_t* sb, uint16_t* C,
+                     int M, int N, int K, int group, unsigned flags, cudaStream_t stream, int32_t* partials_dbg) {
+  g_last_error[0] = '\0';
+  if (flags & ~(ARC_A8W4_PREPACKED | ARC_A8W4_STATIC_WEIGHTS)) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_a8w4_gemm_ex: unknown flags 0x%x", flags);
+  }
+  if ((flags & ARC_A8W4_PREPACKED) && partials_dbg != nullptr) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_a8w4_gemm_ex: no partials dump with pre-packed weights");
+  }
+  return a8w4_gemm(A, sa, Wp, sb, C, M, N, K, group, stream, partials_dbg, nullptr, 0, 0, flags);
+}
+
 int arc_a8w4_gemm_prepacked(const int8_t* A, const float* sa, const uint8_t* Wq, const uint16_t* sb,
                             uint16_t* C, int M, int N, int K, int group, cudaStream_t stream) {
   g_last_error[0] = '\0';
-  return a8w4_gemm(A, sa, Wq, sb, C, M, N, K, group, stream, nullptr, nullptr, 0, 0, 1u);
+  return a8w4_gemm(A, sa, Wq, sb, C, M, N, K, group, stream, nullptr, nullptr, 0, 0, ARC_A8W4_PREPACKED);
 }
 
 int arc_a8w4_prepack_weights(const uint8_t* Wp, uint8_t* Wq, int N, int K, cudaStream_t stream) {
@@ -771,10 +728,13 @@ int arc_a8w4_prepack_weights(const uint8_t* Wp, uint8_t* Wq, int N, int K, cudaS
   return ARC_OK;
 }
 
-int arc_a8w4_gemm_gather(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_t* sb,
-                         uint16_t* const* outs, int world, int rank, int M, int N, int K,
-                         cudaStream_t stream) {
+int arc_a8w4_gemm_gather_ex(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_t* sb,
+                            uint16_t* const* outs, int world, int rank, int M, int N, int K, unsigned flags,
+                            cudaStream_t stream) {
   g_last_error[0] = '\0';
+  if (flags & ~ARC_A8W4_STATIC_WEIGHTS) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_a8w4_gemm_gather_ex: unsupported flags 0x%x", flags);
+  }
   if (outs == nullptr || world < 1 || world > static_cast<int>(arcb::peer::kMaxPeers) || rank < 0 ||
       rank >= world) {
     return fail(ARC_ERR_INVALID_ARGUMENT, "arc_a8w4_gemm_gather: bad outs / world (%d) / rank (%d)", world,
@@ -794,7 +754,13 @@ int arc_a8w4_gemm_gather(const int8_t* A, const float* sa, const uint8_t* Wp, co
     return fail(ARC_ERR_UNSUPPORTED, "arc_a8w4_gemm_gather: N (%d) must be a positive multiple of 8", N);
   }
   return a8w4_gemm(A, sa, Wp, sb, outs[rank] + size_t(rank) * N, M, N, K, 128, stream, nullptr, outs, world,
-                   rank, 0u);
+                   rank, flags);
+}
+
+int arc_a8w4_gemm_gather(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_t* sb,
+                         uint16_t* const* outs, int world, int rank, int M, int N, int K,
+                         cudaStream_t stream) {
+  return arc_a8w4_gemm_gather_ex(A, sa, Wp, sb, outs, world, rank, M, N, K, 0u, stream);
 }
 
 int arc_ipc_export(const void* ptr, void* handle, uint64_t* offset) {
@@ -881,7 +847,7 @@ namespace {
 
 int a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_t* sb, uint16_t* C, int M,
               int N, int K, int group, cudaStream_t stream, int32_t* partials_dbg, uint16_t* const* outs,
-              int world, int rank, uint32_t split) {
+              int world, int rank, uint32_t flags) {
   if (A == nullptr || sa == nullptr || Wp == nullptr || sb == nullptr || C == nullptr) {
     return fail(ARC_ERR_INVALID_ARGUMENT, "arc_a8w4_gemm: null pointer");
   }
@@ -916,11 +882,10 @@ int a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_
   if (M <= static_cast<int>(kDecodeMaxM)) {
     namespace D = arcb::a8w4dec;
     D::Params p;
-    const uint32_t gps = static_cast<uint32_t>(plan.groups_per_stage);
-    if (int st = encode_tokens_3d(&p.tm_tok, A, M, K, BT, gps)) return st;
-    // Packed weights as [N][K/8] u32 so one box row spans gps groups (gps*64 bytes).
-    if (int st = encode_2d(&p.tm_wp, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, Wp, K / 8, N, K / 8,
-                           gps * (arcb::a8w4::kPackedRow / 4), R, CU_TENSOR_MAP_SWIZZLE_NONE,
+    if (int st = encode_tokens_3d(&p.tm_tok, A, M, K, BT, D::kGps)) return st;
+    // Packed weights [N][K/2] bytes; a box row is two K-groups (128 bytes), swizzled.
+    if (int st = encode_2d(&p.tm_wp, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Wp, K / 2, N, K / 2,
+                           D::kGps * arcb::a8w4::kPackedRow, arcb::a8w4::kRows, CU_TENSOR_MAP_SWIZZLE_128B,
                            "Wp")) {
       return st;
     }
@@ -933,7 +898,6 @@ int a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_
       return st;
     }
     p.peers = 0;
-    p.split = split;
     if (outs != nullptr) {
       for (int i = 0; i < world; ++i) {
         if (int st = encode_2d(&p.tm_peer[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
@@ -946,32 +910,22 @@ int a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_
     }
     p.sa = sa;
     p.sb = sb;
-    p.out = C;
     p.partials = partials_dbg;
     p.M = M;
     p.N = N;
     p.K = K;
     p.G = G;
     p.ldsb = G;
-    p.ldc = ldo;
-    p.R = R;
-    p.S = plan.k_split;
+    p.S = S;
     p.num_items = ceil_div(N, R);
-    p.gps = gps;
-    p.stage_bytes = decode_stage_bytes(BT, R, gps);
-    p.stages = plan.load_stages;
-    p.tok_bytes = gps * BT * arcb::a8w4::kGroupK;
-    p.slot_stride = R * arcb::a8w4::kGroupK;
-    p.slots = arcb::a8w4dec::kSlotBytes / p.slot_stride;
-    if (p.slots > arcb::a8w4dec::kMaxSlots) p.slots = arcb::a8w4dec::kMaxSlots;
-    if (p.slots < gps) return fail(ARC_ERR_UNSUPPORTED, "decode plan: too few unpack slots");
+    p.split = (flags & ARC_A8W4_PREPACKED) ? 1u : 0u;
+    p.static_weights = (flags & ARC_A8W4_STATIC_WEIGHTS) ? 1u : 0u;
+    p.sb_vec = (G % 8 == 0 && aligned16(sb)) ? 1u : 0u;
     const uint32_t grid = static_cast<uint32_t>(plan.grid);
     if (BT == 16) {
-      e = launch_ex(D::gemm_a8w4_decode_kernel<16>, p, grid, D::kThreads, decode_smem_bytes<16>(),
-                    p.S, stream);
+      e = launch_ex(D::gemm_a8w4_decode_kernel<16>, p, grid, D::kThreads, decode_smem_bytes<16>(), S, stream);
     } else {
-      e = launch_ex(D::gemm_a8w4_decode_kernel<32>, p, grid, D::kThreads, decode_smem_bytes<32>(),
-                    p.S, stream);
+      e = launch_ex(D::gemm_a8w4_decode_kernel<32>, p, grid, D::kThreads, decode_smem_bytes<32>(), S, stream);
     }
     if (e != cudaSuccess) return cuda_fail(e, "gemm_a8w4_decode_kernel launch");
     return ARC_OK;
@@ -1001,7 +955,7 @@ int a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_
   p.tiles_m = ceil_div(M, BT);
   p.tiles_n = ceil_div(N, R);
   p.num_tiles = p.tiles_m * p.tiles_n;
-  p.split = split;
+  p.split = (flags & ARC_A8W4_PREPACKED) ? 1u : 0u;
   const uint32_t grid = static_cast<uint32_t>(plan.grid);
   if (BT == 64) {
     e = launch_ex(Q::gemm_a8w4_kernel<64, 1, 4>, p, grid, Q::Cfg<64, 1, 4>::kThreads,

@@ -1,35 +1,43 @@
 // gemm_a8w4_decode.cuh — A8W4 GEMM for decode-sized M (<= 32 tokens).
 //
 // Same arithmetic and operand formats as gemm_a8w4.cuh (int8 tokens x int4 weights
-// placed in the high nibble, exact int32 group partials, fp32 scale epilogue), but a
-// decomposition built for streaming the weight matrix once at HBM speed:
+// placed in the high nibble, exact int32 group partials, fp32 scale epilogue), with a
+// decomposition built for streaming the weight matrix once at HBM speed, inside a
+// stream of back-to-back launches:
 //
-// * A CTA owns R weight rows (R <= 128, a multiple of 8) and a K-group range. With
-//   S > 1 (2 or 4) the CTAs of a cluster split K and push fp32 partials to the CTA
-//   that finishes each row through distributed shared memory (the grid is then
-//   exactly one wave); with S == 1 CTAs are persistent over weight tiles. The count
-//   of tcgen05.mma instructions per CTA (four per K-group, each costing tens of
-//   cycles to issue whatever its N) is what the K split spreads out.
-// * Loads are wide: one ring stage holds GPS (2, 4 or 8) consecutive K-groups, fetched
-//   with two TMA instructions — the packed weights as one [R x GPS*64 B] box (a u32
-//   view, so a box row spans GPS groups) and the token tiles as one 3-D box
-//   [GPS][BT][128 B] in the 128-byte swizzle layout the UMMA B operand expects.
-// * Eight unpack warps split a stage by rows (each reads whole contiguous rows) and
-//   write every group into its own unpacked slot. Slots are packed R rows apart:
-//   the UMMA reads 128 rows from a slot base, rows >= R fall into the next slot and
-//   only feed TMEM lanes that are never read. With up to 16 slots a CTA rarely has
-//   to wait for a slot to be released (the wait is on the UMMA completion of the
-//   group that used the slot before).
-// * Every K-group gets its own TMEM accumulator slot (512 / BT of them), so the
-//   tensor core never waits for the epilogue to drain a buffer.
-// * Programmatic dependent launch: the prologue (barrier init, TMEM allocation,
-//   descriptor prefetch) overlaps the previous kernel in the stream;
-//   griddepcontrol.wait precedes every global-memory access.
+// * Every weight tile is 128 rows (TMEM lanes). With S > 1 (2 or 4) the S CTAs of a
+//   cluster split the tile's K-groups and push fp32 partials to the CTA that finishes
+//   each row slice through distributed shared memory (one wave, no global scratch);
+//   with S == 1 CTAs are persistent over weight tiles.
+// * Small footprint, so that the CTAs of the NEXT launch in the stream are resident
+//   while this one runs: <= ~105 KiB of shared memory, 384 threads and 256 TMEM
+//   columns per CTA (two CTAs fit on an SM). The next launch starts at once
+//   (programmatic dependent launch) and, when the caller states that the weights are
+//   not written by the preceding kernel (Params::static_weights), streams its weights
+//   and weight scales and unpacks them BEFORE griddepcontrol.wait. Only the tokens,
+//   the token scales and the output wait for the preceding grid.
+// * Weights move in stages of two K-groups: one TMA box of 128 rows x 128 bytes
+//   (128-byte swizzle). Each thread of the four unpack warps owns one row of a stage and
+//   reads all of it into registers; it writes the first group's 128 int8 codes into a
+//   TMEM slot (one tcgen05.st of 32 columns; the UMMA then takes A from TMEM) and the
+//   second group's back into the same 128 bytes of shared memory, in the swizzled
+//   K-major layout the UMMA reads A from. So the four ring stages hold all eight
+//   K-groups of a decode CTA, unpacked, before the tokens arrive, in 64 KiB of shared
+//   memory plus 128 TMEM columns.
+// * Two UMMA issuer warps take alternate stages (one tcgen05.mma issuing thread needs
+//   ~61 cycles per small UMMA; two keep the tensor pipe near its ~40-cycle floor for
+//   N <= 32, measured on this pool's B200s). A stage is 8 UMMAs, one commit each for
+//   the epilogue, the weight stage and the token stage.
+// * Four epilogue warps read a stage's two int32 partials with one tcgen05.ld (one
+//   TMEM lane = one output column), scale them by sb[n,g] and accumulate in fp32
+//   registers. Every hand-off between roles is paid once per stage, not per group.
 //
-// Roles (512 threads): warp 0 TMA producer, warp 1 UMMA issuer, warp 2 TMEM
-// allocator, warp 3 idle, warps 4-11 unpack, warps 12-15 epilogue (warp 12+q reads
-// TMEM lanes 32q..32q+31, i.e. weight rows 32q..; warps whose rows are all >= R only
-// take part in the barriers).
+// Roles (384 threads): warp 0 TMA producer, warps 1 and 3 UMMA issuers (even / odd
+// stages), warp 2 TMEM allocator, warps 4-7 unpack, warps 8-11 epilogue (warps 4+q and
+// 8+q own TMEM lanes 32q..32q+31).
+//
+// Every wait is bounded (sm100.cuh: mbar_wait); a timeout sets a status bit, lets the
+// CTA's roles leave their loops and still pass every barrier they share.
 #pragma once
 
 #include "gemm_a8w4.cuh"
@@ -42,91 +50,95 @@ using a8w4::expand_piece;
 using a8w4::kGroupK;
 using a8w4::kPackedRow;
 using a8w4::kRows;
-using a8w4::kUmmaK;
 
-constexpr uint32_t kUnpackWarps = 8;
-constexpr uint32_t kEpiWarps = 4;
-constexpr uint32_t kThreads = 32 * (4 + kUnpackWarps + kEpiWarps);
-constexpr uint32_t kMaxStages = 8;
-constexpr uint32_t kRingBytes = 88 * 1024;
-constexpr uint32_t kSlotBytes = 112 * 1024;  // unpacked slots, R*128 bytes apart
-constexpr uint32_t kMaxSlots = 16;
-constexpr uint32_t kScaleLookahead = 8;
-constexpr uint32_t kMaxPeers = 8;  // GPUs of a fused all-gather
+constexpr uint32_t kThreads = 384;
+constexpr uint32_t kTmemCols = 256;   // half an SM's TMEM: two CTAs share one SM
+constexpr uint32_t kGps = 2;          // K-groups per load stage (one 128-byte box row)
+constexpr uint32_t kWStageBytes = kRows * kGps * kPackedRow;  // 16 KiB of packed weights
+constexpr uint32_t kWStages = 4;
+constexpr uint32_t kMaxPeers = 8;     // GPUs of a fused all-gather
+constexpr uint32_t kEpiThread0 = 256; // first thread of the epilogue warps
 
 struct Params {
-  CUtensorMap tm_tok;  // A as [G][M][128] u8 (3-D), box {128, BT, GPS}, SW128
-  CUtensorMap tm_wp;   // Wp as [N][K/8] u32, box {16*GPS, R}, no swizzle
-  CUtensorMap tm_out;  // out [M][N] bf16, box {R / S, BT}, no swizzle
+  CUtensorMap tm_tok;  // A as [G][M][128] u8 (3-D), box {128, BT, 2}, SW128
+  CUtensorMap tm_wp;   // Wp [N][K/2] u8, box {128 B, 128 rows}, SW128
+  CUtensorMap tm_out;  // out [M][N] bf16, box {128 / S, BT}, no swizzle
   const float* sa;
   const uint16_t* sb;
-  uint16_t* out;
   int32_t* partials;   // optional [M][N][G] int32 dump
   uint32_t M, N, K, G;
-  uint32_t ldsb, ldc;
-  uint32_t R;          // weight rows per tile
+  uint32_t ldsb;
   uint32_t S;          // CTAs per cluster along K: 1 (persistent tiles), 2 or 4
-  uint32_t num_items;  // weight tiles
-  uint32_t gps;        // K-groups per ring stage (2, 4 or 8)
-  uint32_t stages;     // ring depth (<= kMaxStages)
-  uint32_t stage_bytes;
-  uint32_t tok_bytes;  // token part of a stage: gps * BT * 128
-  uint32_t slots;      // unpacked slots (<= kMaxSlots)
-  uint32_t slot_stride;  // R * 128 (a multiple of 1024)
+  uint32_t num_items;  // weight tiles of 128 rows
+  uint32_t split;      // Wp in the pre-packed layout (a8w4::expand_piece)
+  uint32_t static_weights;  // Wp and sb are not written by the preceding kernel
+  uint32_t sb_vec;     // sb rows 16-byte aligned with G % 8 == 0: 8 scales per load
   // Fused all-gather (peers > 0): every output tile is stored into each rank's output
   // through tm_peer[i], the [M][N] column window of rank i's gathered [M][world*N] output
   // that this rank owns (peer memory over NVLink; TMA stores only). tm_out is then unused.
   uint32_t peers;
-  uint32_t split;  // Wp in the pre-packed layout (a8w4::expand_piece)
   CUtensorMap tm_peer[kMaxPeers];
 };
 
 template <uint32_t BT>
 struct Cfg {
   static_assert(BT == 16 || BT == 32, "decode token tile");
-  static constexpr uint32_t kTokTile = BT * kGroupK;
-  static constexpr uint32_t kTmemSlots = 512 / BT;
+  static constexpr uint32_t kTokTile = BT * kGroupK;        // one group's token box
+  static constexpr uint32_t kTokStage = kGps * kTokTile;    // 4 or 8 KiB
+  static constexpr uint32_t kTStages = BT == 16 ? 4 : 3;
+  // TMEM: columns [0, 128) hold the first group of each weight stage (32 columns per
+  // group), then kDStages accumulator slots of one stage (2 x BT columns) each.
+  static constexpr uint32_t kDBase = kWStages * 32;
+  static constexpr uint32_t kDStages = BT == 16 ? 4 : 2;
+  static_assert(kDBase + kDStages * 2 * BT <= kTmemCols, "TMEM budget");
 };
 
 template <uint32_t BT>
 struct alignas(1024) Smem {
   using C = Cfg<BT>;
-  // Unpacked slots first: a UMMA on the last slot reads up to 16 KB past its base,
-  // which stays inside this CTA's shared memory (the ring that follows).
-  uint8_t slots[kSlotBytes];
-  uint8_t ring[kRingBytes];                  // stages: [GPS token tiles | R x GPS*64 B]
-  float recv[kRows * BT];                    // [src][R/S][BT] partials from the peers
-  uint64_t load_full[kMaxStages];
-  uint64_t load_empty[kMaxStages];
-  uint64_t unpacked[kMaxStages];             // stage fully unpacked (one arrive per warp)
-  uint64_t mma_done[C::kTmemSlots];
-  uint64_t tmem_empty[C::kTmemSlots];
+  // Packed weights [128 rows][2 groups x 64 B], SW128; after the unpack the second
+  // group's int8 codes [128 rows][128 B] in the same bytes (SW128 K-major, UMMA A).
+  uint8_t wring[kWStages][kWStageBytes];
+  uint8_t tring[C::kTStages][C::kTokStage];     // tokens [2 groups][BT][128 B], SW128
+  float recv[kRows * BT];                       // [src][128 / S][BT] partials from the peers
+  uint64_t w_full[kWStages];
+  uint64_t w_empty[kWStages];                   // the stage's UMMAs retired
+  uint64_t a_full[kWStages];                    // the stage is unpacked
+  uint64_t t_full[C::kTStages];
+  uint64_t t_empty[C::kTStages];
+  uint64_t mma_done[C::kDStages];               // a stage's UMMAs retired
+  uint64_t tmem_empty[C::kDStages];             // its accumulators were read
   uint64_t drain;
-  uint64_t recv_full;                        // peers' partials landed (S > 1)
+  uint64_t recv_full;                           // peers' partials landed (S > 1)
   uint32_t tmem_base;
   uint32_t abort;
 };
 
-struct Item {
-  uint32_t n0, g0, g1;
-};
-
-__device__ __forceinline__ bool get_item(const Params& p, uint32_t idx, Item& it) {
-  if (p.S > 1) {
-    if (idx != 0) return false;
-    const uint32_t rank = blockIdx.x % p.S;
-    it.n0 = (blockIdx.x / p.S) * p.R;
-    it.g0 = rank * p.G / p.S;
-    it.g1 = (rank + 1) * p.G / p.S;
-    return true;
+// The sequence of load stages one CTA works through: `items` weight tiles of `ng`
+// K-groups each (one tile for S > 1), in stages of two consecutive groups of one tile
+// (a tile with an odd group count ends with a one-group stage), flattened.
+struct Walk {
+  uint32_t g0, ng, spi, items;
+  __device__ __forceinline__ explicit Walk(const Params& p) {
+    if (p.S > 1) {
+      const uint32_t r = blockIdx.x % p.S;
+      g0 = r * p.G / p.S;
+      ng = (r + 1) * p.G / p.S - g0;
+      items = 1;
+    } else {
+      g0 = 0;
+      ng = p.G;
+      items = blockIdx.x < p.num_items ? (p.num_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    }
+    spi = (ng + 1) / 2;
   }
-  const uint32_t t = blockIdx.x + idx * gridDim.x;
-  if (t >= p.num_items) return false;
-  it.n0 = t * p.R;
-  it.g0 = 0;
-  it.g1 = p.G;
-  return true;
-}
+  __device__ __forceinline__ uint32_t stages() const { return items * spi; }
+  __device__ __forceinline__ uint32_t n0(const Params& p, uint32_t k) const {
+    return (p.S > 1 ? blockIdx.x / p.S : blockIdx.x + k * gridDim.x) * kRows;
+  }
+  // Stage t covers groups gi = 2*(t % spi) and gi + 1 (if gi + 1 < ng) of tile t / spi.
+  __device__ __forceinline__ bool has_second(uint32_t t) const { return 2u * (t % spi) + 1u < ng; }
+};
 
 // Every lane of the warp waits; the warp proceeds only if all of them succeeded,
 // so a timeout can never split a warp in front of a .sync.aligned instruction.
@@ -135,15 +147,21 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   const bool ok = mbar_wait(bar, parity, abort, err);
   return __all_sync(0xffffffffu, ok);
 }
+// The same, polling (mbar_wait_poll): for the waits on the critical path after the tokens.
+__device__ __forceinline__ bool warp_wait_poll(uint64_t* bar, uint32_t parity, volatile uint32_t* abort,
+                                               uint32_t err) {
+  const bool ok = mbar_wait_poll(bar, parity, abort, err);
+  return __all_sync(0xffffffffu, ok);
+}
 
-__device__ __forceinline__ void st_dsmem_f32x4(uint32_t addr, float a, float b, float c, float d) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b),
-               "f"(c), "f"(d)
-               : "memory");
+// bf16 scale j (0..7) of an 8-scale window, as fp32.
+__device__ __forceinline__ float window_scale(const uint4& w, uint32_t j) {
+  const uint32_t word = (j & 4u) ? ((j & 2u) ? w.w : w.z) : ((j & 2u) ? w.y : w.x);
+  return __uint_as_float((j & 1u) ? (word & 0xFFFF0000u) : (word << 16));
 }
 
 template <uint32_t BT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     gemm_a8w4_decode_kernel(const __grid_constant__ Params p) {
   using C = Cfg<BT>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -151,29 +169,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t warp = warp_idx_sync();
   const uint32_t lane = threadIdx.x & 31u;
   volatile uint32_t* abort = &s.abort;
-  const uint32_t epi_warps = (p.R + 31) / 32;
 
   if (threadIdx.x == 0) probe_mark(0);  // kernel entry
   pdl_launch_dependents();
   if (warp == 0) {
-    // The ~90 barrier inits are spread over the warp's lanes (each is a shared-memory
-    // operation with a long latency).
     if (lane == 0) {
       tma_prefetch_desc(&p.tm_tok);
       tma_prefetch_desc(&p.tm_wp);
       tma_prefetch_desc(&p.tm_out);
     }
-    for (uint32_t i = lane; i < p.stages; i += 32) {
-      mbar_init(&s.load_full[i], 1);
-      mbar_init(&s.load_empty[i], kUnpackWarps + 1);  // each unpack warp + the UMMA commit
-      mbar_init(&s.unpacked[i], kUnpackWarps);
+    // The barrier inits are spread over the warp's lanes (each is a shared-memory
+    // operation with a long latency).
+    for (uint32_t i = lane; i < kWStages; i += 32) {
+      mbar_init(&s.w_full[i], 1);
+      mbar_init(&s.w_empty[i], 1);  // the stage's issuer commits
+      mbar_init(&s.a_full[i], 4);   // the four unpack warps
     }
-    for (uint32_t i = lane; i < C::kTmemSlots; i += 32) {
+    for (uint32_t i = lane; i < C::kTStages; i += 32) {
+      mbar_init(&s.t_full[i], 1);
+      mbar_init(&s.t_empty[i], 1);
+    }
+    for (uint32_t i = lane; i < C::kDStages; i += 32) {
       mbar_init(&s.mma_done[i], 1);
-      mbar_init(&s.tmem_empty[i], epi_warps);
+      mbar_init(&s.tmem_empty[i], 4);  // the four epilogue warps
     }
     if (lane == 0) {
-      mbar_init(&s.drain, 1);
+      mbar_init(&s.drain, 2);
       mbar_init(&s.recv_full, 1);
       s.abort = 0;
     }
@@ -182,11 +203,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && p.S > 1) {
       // Armed before the cluster barrier below, so every peer's bulk copy lands on a
       // barrier that already expects it.
-      mbar_arrive_expect_tx(&s.recv_full, (p.S - 1) * (p.R / p.S) * BT * 4u);
+      mbar_arrive_expect_tx(&s.recv_full, (p.S - 1) * (kRows / p.S) * BT * 4u);
     }
   }
   if (warp == 2) {
-    tmem_alloc(&s.tmem_base, 512);
+    tmem_alloc(&s.tmem_base, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before_sync();
@@ -194,309 +215,335 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after_sync();
   if (p.S > 1) cluster_sync_all();  // every CTA's barriers exist before any exchange
   if (threadIdx.x == 0) probe_mark(1);  // prologue done
-  // Everything above overlaps the previous grid; nothing below may run before it
-  // has completed and its writes are visible.
-  pdl_wait();
-  if (threadIdx.x == 0) probe_mark(2);  // previous grid complete
-  bool cl_arrived = false;  // this thread's arrival on the end-of-kernel cluster barrier
   const uint32_t tmem_base = s.tmem_base;
+  const Walk wk(p);
+  const uint32_t ns = wk.stages();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
+    // Weight stages run up to kWStages ahead of token stages; with static weights the
+    // first kWStages are issued before the wait for the preceding grid.
     if (lane == 0) {
-      const uint32_t tx = p.tok_bytes + p.R * p.gps * kPackedRow;
-      uint32_t q = 0;  // stages issued
-      Item it;
+      uint32_t wi = 0, ti = 0;  // weight / token stages issued
       bool ok = true;
-      for (uint32_t idx = 0; ok && get_item(p, idx, it); ++idx) {
-        for (uint32_t g = it.g0; g < it.g1; g += p.gps, ++q) {
-          const uint32_t st = q % p.stages;
-          // The first fill of each stage needs no wait (a wait on a fresh barrier still
-          // costs ~240 cycles of this thread's time before the first load goes out).
-          if (q >= p.stages && !mbar_wait(&s.load_empty[st], ((q / p.stages) & 1u) ^ 1u, abort,
-                                          kStatusTimeoutProducer)) {
-            ok = false;
-            break;
-          }
-          uint8_t* base = s.ring + st * p.stage_bytes;
-          mbar_arrive_expect_tx(&s.load_full[st], tx);
-          tma_load_3d(&p.tm_tok, &s.load_full[st], base, 0, 0, int32_t(g), kCacheEvictLast);
-          tma_load_2d(&p.tm_wp, &s.load_full[st], base + p.tok_bytes,
-                      int32_t(g * (kPackedRow / 4)), int32_t(it.n0), kCacheEvictFirst);
+      auto issue_w = [&](uint32_t t) -> bool {
+        const uint32_t slot = t % kWStages;
+        if (t >= kWStages &&
+            !mbar_wait(&s.w_empty[slot], ((t / kWStages) & 1u) ^ 1u, abort, kStatusTimeoutProducer)) {
+          return false;
         }
+        mbar_arrive_expect_tx(&s.w_full[slot], kWStageBytes);
+        tma_load_2d(&p.tm_wp, &s.w_full[slot], s.wring[slot], int32_t((wk.g0 + 2u * (t % wk.spi)) * kPackedRow),
+                    int32_t(wk.n0(p, t / wk.spi)), kCacheEvictFirst);
+        return true;
+      };
+      if (p.static_weights) {
+        while (ok && wi < ns && wi < kWStages) ok = issue_w(wi++);
+        probe_mark(2);  // weights issued ahead of the wait
       }
-      probe_mark(3);  // every load issued
-      const uint32_t n_drain = q < p.stages ? q : p.stages;
-      for (uint32_t j = q - n_drain; j < q; ++j) {
-        mbar_drain(&s.load_full[j % p.stages], (j / p.stages) & 1u);
-      }
-      probe_mark(10);  // producer drained
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ UMMA issuer
-    // One thread issues everything. tcgen05.mma issue costs tens of cycles of this
-    // thread's own instruction latency, so the loop keeps ring/slot positions as
-    // wrapping counters (no division) and derives descriptors by adding offsets.
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_s8_s32(kRows, BT);
-      const uint64_t slot_desc0 = make_sw128_kmajor_desc(s.slots);
-      const uint64_t ring_desc0 = make_sw128_kmajor_desc(s.ring);
-      uint32_t st = 0, st_ph = 0;   // ring stage and its phase parity
-      uint32_t ts = 0, ts_ph = 0;   // TMEM accumulator slot and its phase parity
-      uint32_t sl = 0;              // unpacked slot
-      uint32_t q = 0, i = 0;        // stages / groups consumed (probe only)
-      Item it;
-      bool ok = true;
-      for (uint32_t idx = 0; ok && get_item(p, idx, it); ++idx) {
-        for (uint32_t g0 = it.g0; ok && g0 < it.g1; g0 += p.gps, ++q) {
-          // Both tested at once (a test costs ~180 cycles even when complete).
-          const uint32_t t_ld = mbar_test(&s.load_full[st], st_ph);
-          const uint32_t t_up = mbar_test(&s.unpacked[st], st_ph);
-          if ((t_ld == 0u && !mbar_wait(&s.load_full[st], st_ph, abort, kStatusTimeoutMma)) ||
-              (t_up == 0u && !mbar_wait(&s.unpacked[st], st_ph, abort, kStatusTimeoutMma))) {
-            ok = false;
-            break;
-          }
-          probe_mark(8 + (q & 7u));  // stage landed and unpacked
-          tc_fence_after_sync();
-          const uint64_t tok_desc = desc_advance(ring_desc0, st * p.stage_bytes);
-          const uint32_t n_in = min(p.gps, it.g1 - g0);
-#pragma unroll 1
-          for (uint32_t j = 0; j < n_in; ++j, ++i) {
-            // A TMEM slot is waited for only when it has been used before.
-            if (i >= C::kTmemSlots &&
-                !mbar_wait(&s.tmem_empty[ts], ts_ph ^ 1u, abort, kStatusTimeoutMma)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after_sync();
-            const uint64_t adesc = desc_advance(slot_desc0, sl * p.slot_stride);
-            const uint64_t bdesc = desc_advance(tok_desc, j * C::kTokTile);
-            const uint32_t d = tmem_base + ts * BT;
-            umma_s8(d, adesc, bdesc, idesc, 0u);
-            umma_s8(d, desc_advance(adesc, 32), desc_advance(bdesc, 32), idesc, 1u);
-            umma_s8(d, desc_advance(adesc, 64), desc_advance(bdesc, 64), idesc, 1u);
-            umma_s8(d, desc_advance(adesc, 96), desc_advance(bdesc, 96), idesc, 1u);
-            // One commit per group: the epilogue waits on it, and so does the unpack
-            // warp that next writes this group's unpacked slot.
-            umma_commit(&s.mma_done[ts]);
-            probe_mark(32 + (i & 15u));  // group issued to the tensor core
-            if (++ts == C::kTmemSlots) {
-              ts = 0;
-              ts_ph ^= 1u;
-            }
-            if (++sl == p.slots) sl = 0;
-          }
-          if (ok) umma_commit(&s.load_empty[st]);  // token tiles of the stage consumed
-          if (++st == p.stages) {
-            st = 0;
-            st_ph ^= 1u;
-          }
-        }
-      }
-      umma_commit(&s.drain);
-      mbar_drain(&s.drain, 0);
-      probe_mark(11);  // every UMMA retired
-    }
-  } else if (warp >= 4 && warp < 4 + kUnpackWarps) {
-    // ------------------------------------------------------------ unpack warps
-    // A stage row is gps*64 bytes; a lane converts one 16-byte piece (32 codes of
-    // one group) into two 16-byte int8 chunks of that group's slot row.
-    const uint32_t u = warp - 4;
-    const uint32_t row_bytes = p.gps * kPackedRow;
-    const uint32_t lanes_per_row = row_bytes / 16u;     // 16 or 32
-    const uint32_t rows_per_pass = 32u / lanes_per_row; // 2 or 1
-    const uint32_t piece = lane % lanes_per_row;
-    const uint32_t jl = piece >> 2;                     // group within the stage
-    const uint32_t quarter = piece & 3u;                // 32-wide K quarter of the group
-    const uint32_t row0 = u * rows_per_pass + lane / lanes_per_row;
-    const uint32_t row_step = kUnpackWarps * rows_per_pass;
-    uint32_t q = 0, i = 0;
-    Item it;
-    bool ok = true;
-    for (uint32_t idx = 0; ok && get_item(p, idx, it); ++idx) {
-      for (uint32_t g0 = it.g0; ok && g0 < it.g1; g0 += p.gps, ++q) {
-        const uint32_t st = q % p.stages;
-        const uint32_t n_in = min(p.gps, it.g1 - g0);
-        if (!warp_wait(&s.load_full[st], (q / p.stages) & 1u, abort, kStatusTimeoutUnpack)) {
+      // Tokens (and, without static_weights, everything) only after the preceding grid.
+      pdl_wait();
+      probe_mark(3);  // preceding grid complete
+      for (uint32_t t = 0; ok && t < ns; ++t) {
+        while (ok && wi < ns && wi < t + kWStages) ok = issue_w(wi++);
+        if (!ok) break;
+        const uint32_t slot = t % C::kTStages;
+        if (t >= C::kTStages && !mbar_wait(&s.t_empty[slot], ((t / C::kTStages) & 1u) ^ 1u, abort,
+                                           kStatusTimeoutProducer)) {
           ok = false;
           break;
         }
-        // The slots this stage fills are free once the UMMAs of the groups that used
-        // them last (p.slots groups earlier) have completed. Those groups' TMEM slots
-        // cannot have been reused since: their successors come after this unpack.
-        for (uint32_t j = 0; ok && j < n_in; ++j) {
-          const uint32_t gi = i + j;
-          if (gi >= p.slots) {
-            const uint32_t prev = gi - p.slots;
-            ok = warp_wait(&s.mma_done[prev % C::kTmemSlots], (prev / C::kTmemSlots) & 1u, abort,
-                           kStatusTimeoutUnpack);
-          }
+        mbar_arrive_expect_tx(&s.t_full[slot], C::kTokStage);
+        tma_load_3d(&p.tm_tok, &s.t_full[slot], s.tring[slot], 0, 0, int32_t(wk.g0 + 2u * (t % wk.spi)),
+                    kCacheEvictLast);
+        ++ti;
+      }
+      // Every load issued lands before the CTA may exit.
+      for (uint32_t t = wi - (wi < kWStages ? wi : kWStages); t < wi; ++t) {
+        mbar_drain(&s.w_full[t % kWStages], (t / kWStages) & 1u);
+      }
+      for (uint32_t t = ti - (ti < C::kTStages ? ti : C::kTStages); t < ti; ++t) {
+        mbar_drain(&s.t_full[t % C::kTStages], (t / C::kTStages) & 1u);
+      }
+      probe_mark(10);  // producer drained
+    }
+  } else if (warp == 1 || warp == 3) {
+    // ------------------------------------------------------------ UMMA issuers
+    // Issuer q takes the stages t with t % 2 == q. A stage: four K=32 UMMAs of its first
+    // group (A from TMEM) and four of its second (A from the unpacked shared-memory
+    // stage), B from the stage's token tiles, into the accumulator pair of slot
+    // t % kDStages; then one commit each for the epilogue, the weight stage (ring slot
+    // and TMEM A slot free again) and the token stage.
+    if (lane == 0) {
+      // Every wait below depends on the tokens, so it starts after the preceding grid:
+      // a long predecessor can then never run a bounded wait out.
+      pdl_wait();
+      const uint32_t q = warp == 1 ? 0u : 1u;
+      constexpr uint32_t idesc = idesc_s8_s32(kRows, BT);
+      const uint64_t tdesc0 = make_sw128_kmajor_desc(s.tring);
+      const uint64_t wdesc0 = make_sw128_kmajor_desc(s.wring);
+      bool ok = true;
+      for (uint32_t t = q; ok && t < ns; t += 2) {
+        const uint32_t ts = t % C::kTStages, ws = t % kWStages, ds = t % C::kDStages;
+        // The three tests are issued together (each costs ~200 cycles even when complete).
+        const uint32_t t_t = mbar_test(&s.t_full[ts], (t / C::kTStages) & 1u);
+        const uint32_t t_a = mbar_test(&s.a_full[ws], (t / kWStages) & 1u);
+        const uint32_t t_d = t < C::kDStages ? 1u : mbar_test(&s.tmem_empty[ds], ((t / C::kDStages) & 1u) ^ 1u);
+        if ((t_t == 0u && !mbar_wait_poll(&s.t_full[ts], (t / C::kTStages) & 1u, abort, kStatusTimeoutMma)) ||
+            (t_a == 0u && !mbar_wait_poll(&s.a_full[ws], (t / kWStages) & 1u, abort, kStatusTimeoutMma)) ||
+            (t_d == 0u &&
+             !mbar_wait_poll(&s.tmem_empty[ds], ((t / C::kDStages) & 1u) ^ 1u, abort, kStatusTimeoutMma))) {
+          ok = false;
+          break;
         }
-        if (!ok) break;
-        const uint8_t* packed = s.ring + st * p.stage_bytes + p.tok_bytes;
-        if (jl < n_in) {
-          uint8_t* slot = s.slots + ((i + jl) % p.slots) * p.slot_stride;
-#pragma unroll 2
-          for (uint32_t r = row0; r < p.R; r += row_step) {
-            const uint4 x = *reinterpret_cast<const uint4*>(packed + r * row_bytes + piece * 16u);
-            uint4 lo, hi;
-            expand_piece(x, p.split, lo, hi);
-            uint8_t* dst = slot + r * kGroupK;
-            const uint32_t sw = r & 7u;
-            *reinterpret_cast<uint4*>(dst + (((2u * quarter) ^ sw) << 4)) = lo;
-            *reinterpret_cast<uint4*>(dst + (((2u * quarter + 1u) ^ sw) << 4)) = hi;
-          }
+        tc_fence_after_sync();
+        const uint32_t d = tmem_base + C::kDBase + ds * 2u * BT;
+        const uint32_t a = tmem_base + ws * 32u;
+        const uint64_t b = desc_advance(tdesc0, ts * C::kTokStage);
+        umma_s8_tmem_a(d, a, b, idesc, 0u);
+        umma_s8_tmem_a(d, a + 8u, desc_advance(b, 32), idesc, 1u);
+        umma_s8_tmem_a(d, a + 16u, desc_advance(b, 64), idesc, 1u);
+        umma_s8_tmem_a(d, a + 24u, desc_advance(b, 96), idesc, 1u);
+        if (wk.has_second(t)) {
+          const uint64_t w = desc_advance(wdesc0, ws * kWStageBytes);
+          const uint64_t b2 = desc_advance(b, C::kTokTile);
+          umma_s8(d + BT, w, b2, idesc, 0u);
+          umma_s8(d + BT, desc_advance(w, 32), desc_advance(b2, 32), idesc, 1u);
+          umma_s8(d + BT, desc_advance(w, 64), desc_advance(b2, 64), idesc, 1u);
+          umma_s8(d + BT, desc_advance(w, 96), desc_advance(b2, 96), idesc, 1u);
+        }
+        umma_commit(&s.mma_done[ds]);
+        umma_commit(&s.w_empty[ws]);
+        umma_commit(&s.t_empty[ts]);
+        probe_mark(16 + (t & 15u));  // stage issued
+      }
+      umma_commit(&s.drain);
+      mbar_drain(&s.drain, 0);
+      probe_mark(11 + q);  // every UMMA of this issuer retired
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ unpack warps
+    // Thread = row nl of the stage (TMEM lane nl). The row's 128 packed bytes (two
+    // groups, 16-byte chunks placed by the 128-byte swizzle) go to registers; the first
+    // group's 128 int8 codes to TMEM columns [32 * slot, +32), the second's back into the
+    // row's 128 bytes in the K-major SW128 layout.
+    const uint32_t nl = (warp - 4) * 32 + lane;
+    const uint32_t lane_addr = ((warp - 4) * 32u) << 16;
+    const uint32_t sw = nl & 7u;
+    bool ok = true;
+    // With static weights the first kWStages stages are unpacked before the preceding
+    // grid is waited for; every later wait depends on the UMMAs, hence on the tokens.
+    if (!p.static_weights) pdl_wait();
+    for (uint32_t t = 0; ok && t < ns; ++t) {
+      if (p.static_weights && t == kWStages) pdl_wait();
+      const uint32_t ws = t % kWStages;
+      if (!warp_wait(&s.w_full[ws], (t / kWStages) & 1u, abort, kStatusTimeoutUnpack)) {
+        ok = false;
+        break;
+      }
+      uint8_t* row = s.wring[ws] + nl * (kGps * kPackedRow);
+      uint4 x[8];
+#pragma unroll
+      for (uint32_t c = 0; c < 8; ++c) x[c] = *reinterpret_cast<const uint4*>(row + ((c ^ sw) << 4));
+#pragma unroll
+      for (uint32_t h = 0; h < 2; ++h) {  // two 16-column halves of the group (fewer live registers)
+        uint32_t v[16];
+#pragma unroll
+        for (uint32_t c = 0; c < 2; ++c) {
+          uint4 lo, hi;
+          expand_piece(x[2 * h + c], p.split, lo, hi);
+          v[8 * c + 0] = lo.x;
+          v[8 * c + 1] = lo.y;
+          v[8 * c + 2] = lo.z;
+          v[8 * c + 3] = lo.w;
+          v[8 * c + 4] = hi.x;
+          v[8 * c + 5] = hi.y;
+          v[8 * c + 6] = hi.z;
+          v[8 * c + 7] = hi.w;
+        }
+        tmem_st_32x32b_x16(tmem_base + lane_addr + ws * 32u + 16u * h, v);
+      }
+      if (wk.has_second(t)) {
+        // K-major SW128: 16-byte chunk u (k = 16u .. 16u+15) of row nl at (u ^ (nl & 7)).
+#pragma unroll
+        for (uint32_t c = 0; c < 4; ++c) {
+          uint4 lo, hi;
+          expand_piece(x[4 + c], p.split, lo, hi);
+          *reinterpret_cast<uint4*>(row + (((2u * c) ^ sw) << 4)) = lo;
+          *reinterpret_cast<uint4*>(row + (((2u * c + 1u) ^ sw) << 4)) = hi;
         }
         fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&s.unpacked[st]);
-          mbar_arrive(&s.load_empty[st]);
-          if (u == 0) probe_mark(16 + (q & 15u));  // stage unpacked by warp 0
-        }
-        i += n_in;
       }
+      tmem_st_wait();
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.a_full[ws]);
+      if (warp == 4 && lane == 0 && t + 1 == (ns < kWStages ? ns : kWStages)) probe_mark(4);  // first ring unpacked
     }
-  } else if (warp >= 4 + kUnpackWarps) {
+  } else if (warp >= 8) {
     // ------------------------------------------------------------ epilogue warps
-    // All four warps walk the same items and meet at the same named barriers; warps
-    // whose TMEM lanes hold no valid row (and any warp after a failed wait) skip the
-    // arithmetic but not the barriers.
-    const uint32_t qw = warp - (4 + kUnpackWarps);
-    const uint32_t et = threadIdx.x - 32 * (4 + kUnpackWarps);  // 0..127
-    const bool active = qw < epi_warps;
-    const uint32_t nl = qw * 32 + lane;
-    // Lane c holds token c's scale (BT <= 32); loaded now, far from its use.
-    float sa_lane = lane < p.M ? __ldg(p.sa + lane) : 0.f;
-    asm volatile("" : "+f"(sa_lane));
-    const float sa_mine = __shfl_sync(0xffffffffu, sa_lane, lane % BT);  // token et % BT
-    uint32_t i = 0;
-    Item it;
+    const uint32_t qw = warp - 8;
+    const uint32_t et = threadIdx.x - kEpiThread0;  // 0..127
+    const uint32_t nl = qw * 32 + lane;             // row of the tile = TMEM lane
+    const uint32_t lane_addr = (qw * 32u) << 16;
     bool ok = true;
-    for (uint32_t idx = 0; get_item(p, idx, it); ++idx) {
-      const uint32_t n = it.n0 + nl;
-      const bool n_valid = nl < p.R && n < p.N;
-      const uint16_t* sb_row = p.sb + size_t(n_valid ? n : 0) * p.ldsb;
-      float acc[BT];
+
+    // Weight scales of this row for the current tile, 8 K-groups per window: the
+    // current window and the next one are in registers.
+    uint32_t n = wk.n0(p, 0) + nl;
+    bool n_valid = n < p.N;
+    const uint16_t* sb_row = p.sb + size_t(n_valid ? n : 0) * p.ldsb;
+    const bool vec = p.sb_vec != 0u && (wk.g0 & 7u) == 0u;
+    auto load_window = [&](uint32_t w) -> uint4 {
+      uint4 r = make_uint4(0u, 0u, 0u, 0u);
+      if (!n_valid || 8u * w >= wk.ng) return r;
+      const uint16_t* src = sb_row + wk.g0 + 8u * w;
+      if (vec) return __ldg(reinterpret_cast<const uint4*>(src));
+      uint32_t h[8];
 #pragma unroll
-      for (uint32_t j = 0; j < BT; ++j) acc[j] = 0.f;
-      const uint32_t ng = it.g1 - it.g0;
-      if (active && ok) {
-        float sreg[kScaleLookahead];
+      for (uint32_t j = 0; j < 8; ++j) h[j] = 8u * w + j < wk.ng ? __ldg(src + j) : 0u;
+      return make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
+    };
+    // With static weights the scales are loaded before the wait for the preceding grid.
+    if (!p.static_weights) pdl_wait();
+    uint4 win_cur = ns > 0 ? load_window(0) : make_uint4(0u, 0u, 0u, 0u);
+    uint4 win_nxt = ns > 0 ? load_window(1) : win_cur;
+    if (p.static_weights) pdl_wait();  // token scales and outputs only after the preceding grid
+    // Lane c holds token c's scale (BT <= 32).
+    const float sa_lane = lane < p.M ? __ldg(p.sa + lane) : 0.f;
+
+    float acc[BT];
 #pragma unroll
-        for (uint32_t v = 0; v < kScaleLookahead; ++v) {
-          sreg[v] = (n_valid && it.g0 + v < it.g1) ? bf16_bits_to_float(__ldg(sb_row + it.g0 + v))
-                                                   : 0.f;
-        }
-        for (uint32_t jb = 0; ok && jb < ng; jb += kScaleLookahead) {
+    for (uint32_t j = 0; j < BT; ++j) acc[j] = 0.f;
+    for (uint32_t t = 0; t < ns; ++t) {
+      const uint32_t k = t / wk.spi, gi = 2u * (t % wk.spi);
+      const bool second = gi + 1u < wk.ng;
+      if (gi == 0 && k > 0) {  // next tile of a persistent CTA
+        n = wk.n0(p, k) + nl;
+        n_valid = n < p.N;
+        sb_row = p.sb + size_t(n_valid ? n : 0) * p.ldsb;
+        win_cur = load_window(0);
+        win_nxt = load_window(1);
 #pragma unroll
-          for (uint32_t v = 0; v < kScaleLookahead; ++v) {
-            const uint32_t j = jb + v;
-            if (j >= ng) break;
-            const uint32_t ts = i % C::kTmemSlots;
-            const float s_g = sreg[v] * 0.0625f;  // 1/16 undoes the high-nibble placement
-            if (n_valid && j + kScaleLookahead < ng) {
-              sreg[v] = bf16_bits_to_float(__ldg(sb_row + it.g0 + j + kScaleLookahead));
+        for (uint32_t j = 0; j < BT; ++j) acc[j] = 0.f;
+      } else if (gi > 0 && (gi & 7u) == 0u) {
+        win_cur = win_nxt;
+        win_nxt = load_window(gi / 8u + 1u);
+      }
+      const uint32_t ds = t % C::kDStages;
+      if (ok) ok = warp_wait_poll(&s.mma_done[ds], (t / C::kDStages) & 1u, abort, kStatusTimeoutEpilogue);
+      if (ok) {
+        tc_fence_after_sync();
+        const uint32_t dcol = tmem_base + lane_addr + C::kDBase + ds * 2u * BT;
+        // 1/16 undoes the high-nibble placement of the weights.
+        const float s0 = window_scale(win_cur, gi & 7u) * 0.0625f;
+        const float s1 = second ? window_scale(win_cur, (gi + 1u) & 7u) * 0.0625f : 0.f;
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(dcol, r);  // BT=16: both groups; BT=32: the first
+        tmem_ld_wait();
+        if constexpr (BT == 16) {
+          tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.tmem_empty[ds]);
+#pragma unroll
+          for (uint32_t c = 0; c < 16; ++c) acc[c] = fmaf(static_cast<float>(static_cast<int32_t>(r[c])), s0, acc[c]);
+          if (second) {
+#pragma unroll
+            for (uint32_t c = 0; c < 16; ++c) {
+              acc[c] = fmaf(static_cast<float>(static_cast<int32_t>(r[16 + c])), s1, acc[c]);
             }
-            if (!warp_wait(&s.mma_done[ts], (i / C::kTmemSlots) & 1u, abort,
-                           kStatusTimeoutEpilogue)) {
-              ok = false;
-              break;
+          }
+        } else {
+#pragma unroll
+          for (uint32_t c = 0; c < 32; ++c) acc[c] = fmaf(static_cast<float>(static_cast<int32_t>(r[c])), s0, acc[c]);
+          if (p.partials != nullptr && n_valid) {
+            const uint32_t g = wk.g0 + gi;
+#pragma unroll
+            for (uint32_t c = 0; c < 32; ++c) {
+              if (c < p.M) p.partials[(size_t(c) * p.N + n) * p.G + g] = static_cast<int32_t>(r[c]) >> 4;
             }
-            tc_fence_after_sync();
-            uint32_t r[BT];
-            if constexpr (BT == 16) {
-              tmem_ld_32x32b_x16(tmem_base + ((qw * 32u) << 16) + ts * BT, r);
-            } else {
-              tmem_ld_32x32b_x32(tmem_base + ((qw * 32u) << 16) + ts * BT, r);
-            }
+          }
+          if (second) {
+            tmem_ld_32x32b_x32(dcol + 32u, r);
             tmem_ld_wait();
-            tc_fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s.tmem_empty[ts]);
+          }
+          tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.tmem_empty[ds]);
+          if (second) {
 #pragma unroll
-            for (uint32_t c = 0; c < BT; ++c) {
-              acc[c] = fmaf(static_cast<float>(static_cast<int32_t>(r[c])), s_g, acc[c]);
+            for (uint32_t c = 0; c < 32; ++c) {
+              acc[c] = fmaf(static_cast<float>(static_cast<int32_t>(r[c])), s1, acc[c]);
             }
-            if (qw == 0 && lane == 0) probe_mark(48 + (i & 15u));  // group accumulated
-            if (p.partials != nullptr && n_valid) {
-              const uint32_t g = it.g0 + j;
-#pragma unroll
-              for (uint32_t c = 0; c < BT; ++c) {
-                if (c < p.M) {
-                  p.partials[(size_t(c) * p.N + n) * p.G + g] = static_cast<int32_t>(r[c]) >> 4;
-                }
-              }
-            }
-            ++i;
           }
         }
+        if (p.partials != nullptr && n_valid) {
+          // r holds the second group's partials (BT=32), or both groups' (BT=16).
+          const uint32_t g = wk.g0 + gi;
+#pragma unroll
+          for (uint32_t c = 0; c < BT; ++c) {
+            if (c < p.M) {
+              if constexpr (BT == 16) p.partials[(size_t(c) * p.N + n) * p.G + g] = static_cast<int32_t>(r[c]) >> 4;
+              if (second) {
+                p.partials[(size_t(c) * p.N + n) * p.G + g + 1] =
+                    static_cast<int32_t>(r[BT == 16 ? 16 + c : c]) >> 4;
+              }
+            }
+          }
+        }
+        if (qw == 0 && lane == 0) probe_mark(48 + (t & 15u));  // stage accumulated
       }
+      if (gi + 2u < wk.ng) continue;
 
+      // ---------------------------------------------------------- tile complete
+      const uint32_t n0 = wk.n0(p, k);
       if (p.S == 1) {
-        // Whole K range here: scale by sa, stage the [BT][R] bf16 tile, one TMA store.
+        // Whole K range here: scale by sa, stage the [BT][128] bf16 tile, one TMA store.
         uint16_t* tile = reinterpret_cast<uint16_t*>(s.recv);  // recv is unused when S == 1
-        if (et == 0) tma_store_wait_read<0>();  // the previous item's store has read the tile
+        if (et == 0) tma_store_wait_read<0>();  // the previous tile's store has read it
         named_barrier_sync(1, 128);
-        // Every lane takes part in the shuffle (a warp can hold valid and invalid
-        // rows when R is not a multiple of 32); only the store is predicated.
 #pragma unroll
         for (uint32_t c = 0; c < BT; ++c) {
           const float sa_c = __shfl_sync(0xffffffffu, sa_lane, c);
-          if (active && nl < p.R) {
-            tile[c * p.R + nl] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[c] * sa_c));
-          }
+          tile[c * kRows + nl] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[c] * sa_c));
         }
         fence_proxy_async_smem();
         named_barrier_sync(1, 128);
         if (et == 0 && *abort == 0u) {
           if (p.peers == 0) {
-            tma_store_2d(&p.tm_out, tile, int32_t(it.n0), 0);
+            tma_store_2d(&p.tm_out, tile, int32_t(n0), 0);
           } else {
-            for (uint32_t i = 0; i < p.peers; ++i) tma_store_2d(&p.tm_peer[i], tile, int32_t(it.n0), 0);
+            for (uint32_t i = 0; i < p.peers; ++i) tma_store_2d(&p.tm_peer[i], tile, int32_t(n0), 0);
           }
           tma_store_commit();
         }
       } else {
-        // K split over the S-CTA cluster; rank r finishes rows [r*R/S, (r+1)*R/S).
-        // Every row's partial is staged in send[owner][row][token] (the unpacked
-        // slots are idle: every UMMA has completed), the peers' parts are shipped as
-        // one bulk copy per peer into recv[this rank], then all 128 threads sum the
-        // owned slice in rank order and one TMA store writes it.
+        // K split over the S-CTA cluster; rank r finishes rows [r*128/S, (r+1)*128/S).
+        // Every row's partial is staged as send[row][token] in the (now idle) weight
+        // ring, the peers' slices are shipped as one bulk copy per peer into
+        // recv[this rank], then all 128 threads sum the owned slice in rank order and
+        // one TMA store writes it.
         const uint32_t rank = blockIdx.x % p.S;
-        const uint32_t rows_per = p.R / p.S;
-        float* send = reinterpret_cast<float*>(s.slots);
-        uint16_t* tile = reinterpret_cast<uint16_t*>(s.slots + p.R * BT * 4u);
-        if (active && nl < p.R) {
-          const uint32_t owner = nl / rows_per;
-          float4* dst = reinterpret_cast<float4*>(send + (owner * rows_per + nl - owner * rows_per) * BT);
+        const uint32_t rows_per = kRows / p.S;
+        float* send = reinterpret_cast<float*>(s.wring);
+        uint16_t* tile = reinterpret_cast<uint16_t*>(&s.wring[0][0] + kRows * BT * 4u);
+        float4* dst = reinterpret_cast<float4*>(send + nl * BT);
 #pragma unroll
-          for (uint32_t c = 0; c < BT; c += 4) {
-            dst[c / 4] = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
-          }
-        }
+        for (uint32_t c = 0; c < BT; c += 4) dst[c / 4] = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
         fence_proxy_async_smem();
         named_barrier_sync(1, 128);
         if (et == 0 && *abort == 0u) {
-          probe_mark(4);  // partials staged
+          probe_mark(5);  // partials staged
           for (uint32_t o = 0; o < p.S; ++o) {
             if (o == rank) continue;
-            bulk_copy_to_peer(map_to_rank(s.recv + rank * rows_per * BT, o),
-                              send + o * rows_per * BT, rows_per * BT * 4u,
-                              map_to_rank(&s.recv_full, o));
+            bulk_copy_to_peer(map_to_rank(s.recv + rank * rows_per * BT, o), send + o * rows_per * BT,
+                              rows_per * BT * 4u, map_to_rank(&s.recv_full, o));
           }
         }
-        const bool got = warp_wait(&s.recv_full, 0, abort, kStatusTimeoutEpilogue);
-        if (et == 0) probe_mark(5);  // peer partials landed
-        // Nothing targets this CTA's shared memory any more: announce it now and wait at
-        // the end, so the cluster barrier overlaps the reduction and the store.
-        if (!cl_arrived) {
-          __syncwarp();
-          cluster_arrive();
-          cl_arrived = true;
-        }
+        const bool got = warp_wait_poll(&s.recv_full, 0, abort, kStatusTimeoutEpilogue);
+        if (et == 0) probe_mark(6);  // peer partials landed
         if (got) {
+          const float sa_mine = __shfl_sync(0xffffffffu, sa_lane, lane % BT);  // token et % BT
           const float* own = send + rank * rows_per * BT;
           for (uint32_t e = et; e < rows_per * BT; e += 128) {
             const uint32_t rr = e / BT, c = e % BT;  // c == et % BT: sa_mine is its scale
@@ -511,38 +558,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_barrier_sync(1, 128);
         if (et == 0 && *abort == 0u) {
           if (p.peers == 0) {
-            tma_store_2d(&p.tm_out, tile, int32_t(it.n0 + rank * rows_per), 0);
+            tma_store_2d(&p.tm_out, tile, int32_t(n0 + rank * rows_per), 0);
           } else {
             for (uint32_t i = 0; i < p.peers; ++i) {
-              tma_store_2d(&p.tm_peer[i], tile, int32_t(it.n0 + rank * rows_per), 0);
+              tma_store_2d(&p.tm_peer[i], tile, int32_t(n0 + rank * rows_per), 0);
             }
           }
           tma_store_commit();
-          probe_mark(6);  // output store issued
+          probe_mark(7);  // output store issued
         }
       }
     }
-    if (et == 0) tma_store_wait_all<0>();
+    // The stores must have read their shared-memory tile before the CTA exits; their
+    // global writes complete with the grid.
+    if (et == 0) tma_store_wait_read<0>();
   }
 
-  if (warp == 4 && lane == 0) probe_mark(12);  // unpack warp 0 done
-  if (threadIdx.x == 64) probe_mark(15);  // TMEM allocator warp reached the end
   if (p.S > 1) {
-    // No CTA leaves while a bulk copy may still target its shared memory: owners
-    // arrive only after their recv_full wait (or its timeout), every other thread
-    // when its role is done.
+    // No CTA leaves while a peer's bulk copy may still read its shared memory (or write
+    // into it): every thread arrives when its role is done, the epilogue threads after
+    // their recv_full wait. The copies' data is ordered by the transaction counts, so
+    // the arrival orders nothing (relaxed).
     __syncwarp();
-    if (!cl_arrived) cluster_arrive();
+    cluster_arrive_relaxed();
     cluster_wait();
     if (threadIdx.x == 0) probe_mark(14);  // end-of-kernel cluster barrier passed
   }
 
   tc_fence_before_sync();
   __syncthreads();
-  if (threadIdx.x == 0) probe_mark(7);  // teardown
+  if (threadIdx.x == 0) probe_mark(15);  // teardown
   if (warp == 2) {
     tc_fence_after_sync();
-    tmem_dealloc(tmem_base, 512);
+    tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 

@@ -172,6 +172,40 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// The same bounded wait, polling with the non-blocking test instead of letting the
+// thread be suspended: a suspended thread resumes some hundreds of nanoseconds after the
+// phase completes, a polling one within one test (~200 cycles). For the few waits on a
+// short critical path; polling takes issue slots from the other warps of the SM.
+__device__ __forceinline__ bool mbar_wait_poll(uint64_t* bar, uint32_t parity,
+                                               volatile uint32_t* abort, uint32_t err_bit) {
+  const uint32_t addr = smem_u32(bar);
+  uint64_t start = 0;
+#pragma unroll 1
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, P;\n\t}"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((it & 63u) == 0u) {
+      if (it == 0) {
+        start = globaltimer_ns();
+      } else {
+        if (*abort) return false;
+        if (globaltimer_ns() - start > kWaitTimeoutNs) {
+          *abort = 1u;
+          atomicOr(&g_arc_status, err_bit);
+          return false;
+        }
+      }
+    }
+  }
+}
+
 // Non-blocking test of a phase (acquire when it reports completion). On B200 even a
 // test of an already-completed phase takes ~180 cycles to answer, so code that
 // checks several barriers issues all the tests first and lets their latencies
@@ -357,6 +391,19 @@ __device__ __forceinline__ void umma_s8(uint32_t d_tmem, uint64_t a_desc, uint64
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] x B[smem desc]^T, s8 inputs, s32 accumulation. A (M=128) sits in
+// TMEM with row m in lane m and K along the columns, four int8 per 32-bit column in
+// ascending K (byte 0 = lowest k): a K=32 step reads 8 consecutive columns from a_tmem.
+__device__ __forceinline__ void umma_s8_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on `bar` (once) when every tcgen05 operation issued so far by this thread
 // has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -417,6 +464,27 @@ __device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, const uint32_t
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
                "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
                : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+      "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+      "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
 }
 
 __device__ __forceinline__ void tmem_st_wait() {
@@ -487,6 +555,12 @@ __device__ __forceinline__ void cluster_arrive() {
 }
 __device__ __forceinline__ void cluster_wait() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrival that orders no memory: for a barrier that only marks an event whose data is
+// synchronised otherwise (e.g. by mbarrier transaction counts). A release arrival at
+// cluster scope costs the arriving warp on the order of a thousand cycles.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
 
 // Address of the same shared-memory object in CTA `rank` of this cluster.

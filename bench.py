@@ -323,7 +323,8 @@ def run_ours(args, wl, world, rank, local):
         in_bytes = step_bytes - 2 * M * N
 
         def call(s):
-            return arc.a8w4_matmul(s[0], s[1], s[2], prepacked=args.prepacked)
+            # Model weights are written once, never by the kernel before a GEMM.
+            return arc.a8w4_matmul(s[0], s[1], s[2], prepacked=args.prepacked, static_weights=True)
     elif wl["kind"] == "fp8fp4":
         step_bytes = fp8fp4_bytes(M, N, K)
         in_bytes = step_bytes - 2 * M * N
@@ -395,7 +396,7 @@ def run_ours(args, wl, world, rank, local):
         launches_per_step = 2
 
         def call(s):
-            return fused.matmul(s[0], s[1])
+            return fused.matmul(s[0], s[1], static_weights=True)
     # The fused gather's barrier keeps its epoch on the device, so its steps capture into
     # a graph like the GEMM alone; the NCCL gather runs eagerly.
     use_graph = flush is None and not args.no_graph and gather != "nccl"

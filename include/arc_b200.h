@@ -93,6 +93,28 @@ int arc_a8w4_gemm(const int8_t *A, const float *sa, const uint8_t *Wp, const uin
                   int32_t *partials_dbg);
 
 /*
+ * arc_a8w4_gemm with flags (the reference's call has none; same role, tests/a8w4.py:48).
+ *   ARC_A8W4_PREPACKED       Wp is in the layout of arc_a8w4_prepack_weights (no partials
+ *                            dump then).
+ *   ARC_A8W4_STATIC_WEIGHTS  Wp and sb are not written by the kernel that directly precedes
+ *                            this call on `stream`. Every A8W4 kernel is launched with
+ *                            programmatic dependent launch: it may start while the
+ *                            preceding kernel still runs and reads A and sa, and writes C,
+ *                            only after that kernel has completed. With this flag the
+ *                            decode kernel (M <= 32) also streams and unpacks Wp and sb
+ *                            before that point, so consecutive GEMMs on one stream overlap
+ *                            their weight traffic. Weights written by any earlier work
+ *                            (an upload, a copy, a kernel before the preceding one) are
+ *                            fine. Without the flag nothing is read before the preceding
+ *                            kernel completes.
+ */
+#define ARC_A8W4_PREPACKED 1u
+#define ARC_A8W4_STATIC_WEIGHTS 2u
+int arc_a8w4_gemm_ex(const int8_t *A, const float *sa, const uint8_t *Wp, const uint16_t *sb,
+                     uint16_t *C, int M, int N, int K, int group, unsigned flags, cudaStream_t stream,
+                     int32_t *partials_dbg);
+
+/*
  * Weight pre-pack (no reference counterpart: the reference stores weights only in the
  * packing of arc/testing/quant.py:82-83, which Wp above follows). Reorders the nibbles
  * inside every 16-byte piece of Wp [N][K/2] (32 codes, k = 32q .. 32q+31) so that byte j
@@ -115,7 +137,7 @@ int arc_a8w4_gemm_prepacked(const int8_t *A, const float *sa, const uint8_t *Wq,
 typedef struct arc_a8w4_plan {
   int split;        /* 1: K-split clusters with on-chip reduction; 0: persistent tiles */
   int token_tile;   /* tokens (rows of A) per tile: 16, 32, 64 or 128 */
-  int weight_rows;  /* weight rows (output columns) per tile, <= 128 */
+  int weight_rows;  /* weight rows (output columns) per tile: 128 */
   int k_split;      /* CTAs per cluster along K (split == 1) */
   int grid;         /* CTAs launched */
   int load_stages;  /* depth of the TMA ring */
@@ -138,6 +160,12 @@ int arc_a8w4_describe_plan(int M, int N, int K, int num_sms, arc_a8w4_plan_t *pl
 int arc_a8w4_gemm_gather(const int8_t *A, const float *sa, const uint8_t *Wp, const uint16_t *sb,
                          uint16_t *const *outs, int world, int rank, int M, int N, int K,
                          cudaStream_t stream);
+
+/* arc_a8w4_gemm_gather with the flags of arc_a8w4_gemm_ex (ARC_A8W4_STATIC_WEIGHTS; the
+ * fused gather takes weights in the reference packing only). */
+int arc_a8w4_gemm_gather_ex(const int8_t *A, const float *sa, const uint8_t *Wp, const uint16_t *sb,
+                            uint16_t *const *outs, int world, int rank, int M, int N, int K,
+                            unsigned flags, cudaStream_t stream);
 
 /*
  * Stream-ordered barrier of the ranks of a fused all-gather. flags[i] is rank i's array

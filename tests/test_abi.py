@@ -94,11 +94,19 @@ def test_invalid_arguments_are_rejected_before_any_cuda_call(native_lib):
 
 
 @pytest.mark.parametrize("m,n,k,expect", [
-    # decode: 32 full-height tiles, K split four ways in 4-CTA clusters (one wave)
+    # decode: 32 full-height tiles, K split four ways in 4-CTA clusters (one wave, at most
+    # one CTA per SM so that the next launch in the stream fits beside it)
     (16, 4096, 4096, dict(split=1, token_tile=16, weight_rows=128, k_split=4, grid=128)),
+    # 37 tiles x 4 = 148 CTAs still fit; 38 tiles drop to a split of two
+    (16, 4736, 4096, dict(split=1, k_split=4, grid=148)),
+    (16, 4864, 4096, dict(split=1, k_split=2, grid=76)),
     # large N: persistent unsplit 128-row tiles
     (1, 28672, 8192, dict(split=0, token_tile=16, weight_rows=128, grid=148)),
-    (32, 4096, 4096, dict(split=1, token_tile=32)),
+    (16, 14336, 4096, dict(split=0, k_split=1, grid=112)),
+    (32, 4096, 4096, dict(split=1, token_tile=32, k_split=4)),
+    # K of one or two groups limits the split
+    (16, 512, 128, dict(split=0, k_split=1, grid=4)),
+    (16, 512, 256, dict(split=1, k_split=2, grid=8)),
     (33, 4096, 4096, dict(split=0, token_tile=64)),
     (4096, 14336, 4096, dict(split=0, token_tile=128, weight_rows=128, grid=148)),
 ])
@@ -107,21 +115,15 @@ def test_plans(native_lib, m, n, k, expect):
     for key, v in expect.items():
         assert plan[key] == v, (key, plan)
     if m <= 32:
-        assert plan["weight_rows"] % 8 == 0 and (plan["weight_rows"] // plan["k_split"]) % 8 == 0
+        assert plan["weight_rows"] == 128
         assert plan["k_split"] in (1, 2, 4) and plan["k_split"] <= k // 128
-        tiles = -(-n // plan["weight_rows"])
+        tiles = -(-n // 128)
         if plan["split"]:
             assert plan["grid"] == tiles * plan["k_split"] <= 148
         else:
             assert plan["grid"] == min(tiles, 148)
-        # a ring stage is gps token tiles plus gps*64 bytes of each packed row, 1 KB
-        # aligned; gps is the largest of 8, 4, 2 for which two stages fit the 88 KB ring
-        def stage(gps):
-            raw = gps * (plan["token_tile"] * 128 + plan["weight_rows"] * 64)
-            return -(-raw // 1024) * 1024
-        gps = next((g for g in (8, 4) if 88 * 1024 // stage(g) >= 2), 2)
-        assert plan["groups_per_stage"] == gps
-        assert plan["load_stages"] == min(8, 88 * 1024 // stage(gps)) >= 2
+        # weights stream in stages of two K-groups (a 128-byte box row) through 4 stages
+        assert plan["groups_per_stage"] == 2 and plan["load_stages"] == 4
 
 
 def test_decode_plans_cover_every_row(native_lib):

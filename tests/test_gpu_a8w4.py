@@ -171,14 +171,56 @@ def test_a8w4_large_weight_sweep(cuda_device, m):
     assert ok, msg
 
 
-@pytest.mark.parametrize("plan", ["128:4", "128:2", "64:2", "96:4", "64:1", "32:1", "104:1", "48:2"])
+@pytest.mark.parametrize("plan", ["128:4", "128:2", "128:1", "128:1:3", "128:1:1"])
 def test_a8w4_decode_decompositions(cuda_device, monkeypatch, plan):
-    """Every decode decomposition (tile height R, K split S) is exact; forced per test."""
+    """Every decode decomposition is exact; forced per test. K split over 4- and 2-CTA
+    clusters, persistent unsplit tiles, and persistent CTAs capped at 3 and 1 so that each
+    walks several tiles (the A slots, load stages and accumulators carry over between
+    tiles). K = 384 and 640 give one-group load stages and uneven splits."""
     monkeypatch.setenv("ARC_DECODE_PLAN", plan)
-    R, S = (int(v) for v in plan.split(":"))
-    for m, n, k in ((16, 1000, 1024), (3, 512, 2048), (32, 256, 512)):
-        (x, sa, wp, sb), out, parts = _run(cuda_device, m, n, k, seed=R + S + m)
-        assert np.array_equal(parts.cpu().numpy(), oracle.a8w4_partials(x.numpy(), wp.numpy()))
-        ref = oracle.a8w4_out(x.numpy(), sa.numpy(), wp.numpy(), _bits(sb))
-        ok, msg = oracle.check_bf16_close(out.float().cpu().numpy(), ref, max_ulp=2.0)
-        assert ok, f"plan {plan} {m}x{n}x{k}: {msg}"
+    S = int(plan.split(":")[1])
+    for m, n, k in ((16, 1000, 1024), (3, 512, 2048), (32, 256, 512), (16, 1000, 384), (7, 264, 640)):
+        for static in (False, True):
+            (x, sa), (wp, sb) = generate_a8w4(m, n, k, seed=S + m + k)
+            dev = cuda_device
+            parts = torch.full((m, n, k // 128), -12345, dtype=torch.int32, device=dev)
+            out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=dev)
+            arc.a8w4_matmul((x.to(dev), sa.to(dev)), (wp.to(dev), sb.to(dev)), out, partials=parts,
+                            static_weights=static)
+            torch.cuda.synchronize()
+            assert arc.device_status(0) == 0, "kernel reported a wait timeout"
+            assert np.array_equal(parts.cpu().numpy(), oracle.a8w4_partials(x.numpy(), wp.numpy())), \
+                f"plan {plan} {m}x{n}x{k} static={static}: partials differ"
+            ref = oracle.a8w4_out(x.numpy(), sa.numpy(), wp.numpy(), _bits(sb))
+            ok, msg = oracle.check_bf16_close(out.float().cpu().numpy(), ref, max_ulp=2.0)
+            assert ok, f"plan {plan} {m}x{n}x{k} static={static}: {msg}"
+
+
+@pytest.mark.parametrize("m,n,k", [(16, 4096, 4096), (32, 1000, 1024), (1, 28672, 8192)])
+def test_a8w4_static_weights_back_to_back(cuda_device, m, n, k):
+    """static_weights: consecutive decode GEMMs on one stream, each reading tokens that
+    the kernel directly before it wrote (the GPU int8 quantizer). The GEMM streams its
+    weights while the quantizer still runs, but must read the tokens only after it: every
+    result equals the same GEMM run in isolation, bit for bit, and the oracle."""
+    dev = cuda_device
+    (_, _), (wp, sb) = generate_a8w4(m, n, k, seed=11)
+    wpd, sbd = wp.to(dev), sb.to(dev)
+    g = torch.Generator(device=dev).manual_seed(5)
+    xs = [torch.randn(m, k, generator=g, device=dev, dtype=torch.bfloat16) for _ in range(6)]
+    qs = [(torch.empty((m, k), dtype=torch.int8, device=dev), torch.empty((m,), dtype=torch.float32, device=dev))
+          for _ in xs]
+    outs = [torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=dev) for _ in xs]
+    for x, q, o in zip(xs, qs, outs):  # quantize -> GEMM -> quantize -> GEMM ..., no syncs
+        arc.quantize_int8(x, out=q)
+        arc.a8w4_matmul(q, (wpd, sbd), o, static_weights=True)
+    torch.cuda.synchronize()
+    assert arc.device_status(0) == 0, "kernel reported a wait timeout"
+    for i, (q, o) in enumerate(zip(qs, outs)):
+        ref = arc.a8w4_matmul(q, (wpd, sbd))
+        torch.cuda.synchronize()
+        assert torch.equal(o.view(torch.int16), ref.view(torch.int16)), f"call {i} differs"
+    cols = np.sort(np.random.default_rng(3).choice(n, size=min(n, 192), replace=False))
+    q, sa = (t.cpu() for t in qs[-1])
+    want = oracle.a8w4_out(q.numpy(), sa.numpy(), wp.numpy()[cols], _bits(sb)[cols])
+    ok, msg = oracle.check_bf16_close(outs[-1].float().cpu().numpy()[:, cols], want, max_ulp=2.0)
+    assert ok, msg
