@@ -22,6 +22,8 @@ CSRC = ROOT / "csrc"
 INCLUDE = ROOT.parent / "include"
 LIB_PATH = PKG_DIR / "libarcb200.so"
 PROBE_LIB_PATH = PKG_DIR / "libarcb200_probe.so"
+TVM_FFI_LIB_PATH = PKG_DIR / "libarcb200_tvm_ffi.so"
+TVM_FFI_SOURCE = "tvm_ffi_shim.cc"
 STAMP = ROOT / "_build" / "libarcb200.hash"
 
 SOURCES = ["api.cu"]
@@ -93,7 +95,46 @@ def build(force: bool = False, verbose: bool = False, probe: bool = False) -> Pa
     return lib
 
 
+def build_tvm_ffi(force: bool = False) -> Path | None:
+    """Compile libarcb200_tvm_ffi.so: TVM-FFI typed exports (matmul, a8w4_matmul,
+    fp8_fp4_gemm_nt) over the C ABI, the binding shape of the reference
+    (arc/mm.py:30,48). Host C++ only (g++), linked against libarcb200.so, libtvm_ffi.so
+    and the CUDA runtime. Returns None when the tvm_ffi package is not installed: the
+    C ABI and the ctypes layer do not depend on it.
+    """
+    try:
+        import tvm_ffi.libinfo as info
+    except ImportError:
+        return None
+    lib = build()
+    src = CSRC / TVM_FFI_SOURCE
+    stamp = STAMP.with_name("libarcb200_tvm_ffi.hash")
+    h = hashlib.sha256(src.read_bytes() + (INCLUDE / "arc_b200.h").read_bytes()).hexdigest()
+    if not force and TVM_FFI_LIB_PATH.exists() and stamp.exists() and stamp.read_text().strip() == h:
+        return TVM_FFI_LIB_PATH
+    cxx = shutil.which("g++") or shutil.which("c++")
+    if cxx is None:
+        raise RuntimeError("no C++ compiler for the TVM-FFI shim")
+    cuda_home = Path(find_nvcc()).resolve().parent.parent
+    tvm_lib = Path(info.find_libtvm_ffi()).parent
+    tmp = TVM_FFI_LIB_PATH.with_suffix(".so.tmp")
+    cmd = [cxx, "-std=c++17", "-O2", "-fPIC", "-shared", "-o", str(tmp), str(src),
+           "-I", str(INCLUDE), "-I", info.find_include_path(), "-I", info.find_dlpack_include_path(),
+           "-I", str(cuda_home / "include"),
+           "-L", str(lib.parent), "-larcb200", "-L", str(tvm_lib), "-ltvm_ffi",
+           "-L", str(cuda_home / "lib64"), "-lcudart",
+           "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{tvm_lib}", f"-Wl,-rpath,{cuda_home / 'lib64'}"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"TVM-FFI shim build failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    tmp.replace(TVM_FFI_LIB_PATH)
+    stamp.parent.mkdir(parents=True, exist_ok=True)
+    stamp.write_text(h)
+    return TVM_FFI_LIB_PATH
+
+
 if __name__ == "__main__":
     import sys
 
     print(build(force=True, verbose=True, probe="--probe" in sys.argv))
+    print(build_tvm_ffi(force=True))

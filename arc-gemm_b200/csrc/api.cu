@@ -327,6 +327,7 @@ uint32_t ceil_div(uint32_t a, uint32_t b) { return (a + b - 1) / b; }
 // A8W4 work decomposition
 // ---------------------------------------------------------------------------------
 constexpr uint32_t kDecodeMaxM = 32;
+constexpr uint32_t kDecodeLongG = 32;  // K-groups per tile from which persistent plans use 2 CTAs/SM
 
 // Decode-sized problems (M <= 32) stream the weights once, in 128-row tiles. A plan is a
 // K split S in {1, 2, 4}: S > 1 runs one wave of S-CTA clusters that reduce on chip
@@ -366,7 +367,11 @@ int plan_a8w4(int M, int N, int K, int sms, int max_c2, int max_c4, arc_a8w4_pla
         return ARC_OK;
       }
     }
-    decode_plan(bt, 1, tiles < static_cast<uint32_t>(sms) ? tiles : static_cast<uint32_t>(sms), plan);
+    // Persistent tiles. A CTA keeps four 16 KiB weight stages in flight; problems long
+    // enough to be bound by HBM rather than by the launch chain (many K-groups per tile)
+    // run two CTAs per SM, twice the bytes in flight per SM.
+    const uint32_t cap = static_cast<uint32_t>(sms) * (G >= kDecodeLongG ? 2u : 1u);
+    decode_plan(bt, 1, tiles < cap ? tiles : cap, plan);
     return ARC_OK;
   }
   const uint32_t bt = M <= 64 ? 64u : 128u;
@@ -508,6 +513,28 @@ SplitPlan fp8fp4_split_plan(int dev, int M, int N, int K) {
   sp.partial_offset = kSplitCounterBytes;
   sp.bytes = kSplitCounterBytes + size_t(S) * M * N * sizeof(float);
   return sp;
+}
+
+// Argument checks of the FP8 x FP4 entry points (host only: no device call, nothing enqueued).
+int fp8fp4_check(const uint8_t* A, const float* sfa, const uint8_t* Wp, const float* sfw, const uint16_t* C,
+                 int M, int N, int K) {
+  if (A == nullptr || sfa == nullptr || Wp == nullptr || sfw == nullptr || C == nullptr) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_fp8_fp4_gemm: null pointer");
+  }
+  if (M <= 0 || N <= 0 || K <= 0) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_fp8_fp4_gemm: sizes must be positive (M=%d N=%d K=%d)",
+                M, N, K);
+  }
+  if (K % 128 != 0 || N % 8 != 0) {
+    return fail(ARC_ERR_UNSUPPORTED, "arc_fp8_fp4_gemm: need K %% 128 == 0 and N %% 8 == 0 (N=%d K=%d)",
+                N, K);
+  }
+  if (!aligned16(A) || (reinterpret_cast<uintptr_t>(Wp) & 31u) || !aligned16(C) || !aligned16(sfw) ||
+      (reinterpret_cast<uintptr_t>(sfa) & 3u)) {
+    return fail(ARC_ERR_UNSUPPORTED,
+                "arc_fp8_fp4_gemm: A, C and sfw must be 16-byte aligned, Wp 32-byte (sfa 4-byte)");
+  }
+  return ARC_OK;
 }
 
 int fp8fp4_gemm(const uint8_t* A, const float* sfa, const uint8_t* Wp, const float* sfw, uint16_t* C,
@@ -1009,7 +1036,8 @@ int arc_fp8_fp4_gemm_ws(const uint8_t* A, const float* sfa, const uint8_t* Wp, c
 // the operator nothing beyond its input and output tensors, and hosts that must not call
 // cudaMalloc on the request path (it can synchronise the device and its latency is not
 // bounded). For them the K split's scratch lives in a fixed device array built into the
-// library, 4 MiB on every GPU that loads it, held until the process exits.
+// library, 4 MiB on every GPU that loads it, held until the process exits. Shapes whose
+// split would need more run without the split (no scratch).
 // ---------------------------------------------------------------------------------
 namespace {
 
@@ -1032,23 +1060,16 @@ extern "C" int arc_fp8_fp4_gemm_noalloc(const uint8_t* A, const float* sfa, cons
                                         const float* sfw, uint16_t* C, int M, int N, int K,
                                         cudaStream_t stream) {
   g_last_error[0] = '\0';
-  if (M <= 0 || N <= 0 || K <= 0 || K % 128 != 0) {
-    return fail(ARC_ERR_INVALID_ARGUMENT,
-                "arc_fp8_fp4_gemm_noalloc: need positive sizes and K %% 128 == 0 (M=%d N=%d K=%d)", M, N,
-                K);
-  }
+  // Every argument is checked before anything is put on the stream.
+  if (int st = fp8fp4_check(A, sfa, Wp, sfw, C, M, N, K)) return st;
   int dev = 0;
   if (int st = current_device(&dev)) return st;
   int variant = 0;
   if (int st = choose_fp8fp4(dev, M, N, K, aligned16(sfa), &variant)) return st;
   const size_t need = variant == 0 ? fp8fp4_split_plan(dev, M, N, K).bytes : 0;
-  if (need > kNoAllocScratchBytes) {
-    return fail(ARC_ERR_UNSUPPORTED,
-                "arc_fp8_fp4_gemm_noalloc: M=%d N=%d K=%d needs %zu bytes of scratch for its K split; the "
-                "built-in scratch holds %zu (use arc_fp8_fp4_gemm_ws with a workspace of your own)",
-                M, N, K, need, kNoAllocScratchBytes);
-  }
-  if (need == 0) {  // no K split for this shape: no scratch either
+  // No K split for this shape, or one whose partials would not fit the built-in array:
+  // the unsplit kernel, which needs no scratch at all.
+  if (need == 0 || need > kNoAllocScratchBytes) {
     return fp8fp4_gemm(A, sfa, Wp, sfw, C, M, N, K, nullptr, 0, stream);
   }
   NoAllocScratch& sc = g_noalloc[dev];
@@ -1070,22 +1091,7 @@ namespace {
 
 int fp8fp4_gemm(const uint8_t* A, const float* sfa, const uint8_t* Wp, const float* sfw, uint16_t* C,
                 int M, int N, int K, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  if (A == nullptr || sfa == nullptr || Wp == nullptr || sfw == nullptr || C == nullptr) {
-    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_fp8_fp4_gemm: null pointer");
-  }
-  if (M <= 0 || N <= 0 || K <= 0) {
-    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_fp8_fp4_gemm: sizes must be positive (M=%d N=%d K=%d)",
-                M, N, K);
-  }
-  if (K % 128 != 0 || N % 8 != 0) {
-    return fail(ARC_ERR_UNSUPPORTED, "arc_fp8_fp4_gemm: need K %% 128 == 0 and N %% 8 == 0 (N=%d K=%d)",
-                N, K);
-  }
-  if (!aligned16(A) || (reinterpret_cast<uintptr_t>(Wp) & 31u) || !aligned16(C) || !aligned16(sfw) ||
-      (reinterpret_cast<uintptr_t>(sfa) & 3u)) {
-    return fail(ARC_ERR_UNSUPPORTED,
-                "arc_fp8_fp4_gemm: A, C and sfw must be 16-byte aligned, Wp 32-byte (sfa 4-byte)");
-  }
+  if (int st = fp8fp4_check(A, sfa, Wp, sfw, C, M, N, K)) return st;
   int dev = 0;
   if (int st = current_device(&dev)) return st;
   namespace F = arcb::fp8fp4;

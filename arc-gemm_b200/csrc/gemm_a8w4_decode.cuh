@@ -297,20 +297,19 @@ __global__ void __launch_bounds__(kThreads, 2)
           break;
         }
         tc_fence_after_sync();
+        probe_mark(24 + (t & 7u));  // stage's waits passed
         const uint32_t d = tmem_base + C::kDBase + ds * 2u * BT;
         const uint32_t a = tmem_base + ws * 32u;
         const uint64_t b = desc_advance(tdesc0, ts * C::kTokStage);
-        umma_s8_tmem_a(d, a, b, idesc, 0u);
-        umma_s8_tmem_a(d, a + 8u, desc_advance(b, 32), idesc, 1u);
-        umma_s8_tmem_a(d, a + 16u, desc_advance(b, 64), idesc, 1u);
-        umma_s8_tmem_a(d, a + 24u, desc_advance(b, 96), idesc, 1u);
-        if (wk.has_second(t)) {
-          const uint64_t w = desc_advance(wdesc0, ws * kWStageBytes);
-          const uint64_t b2 = desc_advance(b, C::kTokTile);
-          umma_s8(d + BT, w, b2, idesc, 0u);
-          umma_s8(d + BT, desc_advance(w, 32), desc_advance(b2, 32), idesc, 1u);
-          umma_s8(d + BT, desc_advance(w, 64), desc_advance(b2, 64), idesc, 1u);
-          umma_s8(d + BT, desc_advance(w, 96), desc_advance(b2, 96), idesc, 1u);
+        // The two groups' K steps alternate, so consecutive UMMAs accumulate into
+        // different TMEM columns and the tensor pipe never waits on the previous one.
+        const bool two = wk.has_second(t);
+        const uint64_t w = desc_advance(wdesc0, ws * kWStageBytes);
+        const uint64_t b2 = desc_advance(b, C::kTokTile);
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+          umma_s8_tmem_a(d, a + 8u * j, desc_advance(b, 32 * j), idesc, j > 0 ? 1u : 0u);
+          if (two) umma_s8(d + BT, desc_advance(w, 32 * j), desc_advance(b2, 32 * j), idesc, j > 0 ? 1u : 0u);
         }
         umma_commit(&s.mma_done[ds]);
         umma_commit(&s.w_empty[ws]);
@@ -409,8 +408,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     uint4 win_cur = ns > 0 ? load_window(0) : make_uint4(0u, 0u, 0u, 0u);
     uint4 win_nxt = ns > 0 ? load_window(1) : win_cur;
     if (p.static_weights) pdl_wait();  // token scales and outputs only after the preceding grid
-    // Lane c holds token c's scale (BT <= 32).
-    const float sa_lane = lane < p.M ? __ldg(p.sa + lane) : 0.f;
+    // Lane c holds token c's scale (BT <= 32). Waited for here, where the tokens are
+    // still on their way, rather than at its first use at the end of the tile.
+    float sa_lane = lane < p.M ? __ldg(p.sa + lane) : 0.f;
+    asm volatile("" : "+f"(sa_lane));
 
     float acc[BT];
 #pragma unroll
@@ -554,8 +555,10 @@ __global__ void __launch_bounds__(kThreads, 2)
             tile[c * rows_per + rr] = __bfloat16_as_ushort(__float2bfloat16_rn(sum * sa_mine));
           }
         }
+        if (et == 0) probe_mark(8);  // owned slice summed
         fence_proxy_async_smem();
         named_barrier_sync(1, 128);
+        if (et == 0) probe_mark(9);  // tile complete
         if (et == 0 && *abort == 0u) {
           if (p.peers == 0) {
             tma_store_2d(&p.tm_out, tile, int32_t(n0 + rank * rows_per), 0);

@@ -242,13 +242,14 @@ int arc_fp8_fp4_workspace_bytes(int M, int N, int K, size_t *bytes);
  * device and its latency is unbounded). Operands and output are the caller's, as in
  * arc_fp8_fp4_gemm. The K split of decode-sized problems keeps its partials and tile
  * counters in a 4 MiB array built into the library, which every GPU that loads the
- * library holds until the process exits; shapes whose split needs more than that
- * (4096 + S*M*N*4 bytes, S the split count) are rejected with ARC_ERR_UNSUPPORTED and a
- * message naming the size. The first call on a device looks up that device's address
- * of the array (cudaGetSymbolAddress) and should come before any stream capture. Every
- * call uses the same array and clears its counters on `stream` first, so calls whose
- * kernels overlap on the GPU (other streams, other host threads) race and give wrong
- * results: issue them in one stream order.
+ * library holds until the process exits; shapes whose split would need more than that
+ * (4096 + S*M*N*4 bytes, S the split count) run without the split, like
+ * arc_fp8_fp4_gemm. Every argument is checked before anything is enqueued. The first
+ * call on a device looks up that device's address of the array (cudaGetSymbolAddress)
+ * and should come before any stream capture. Every call uses the same array and clears
+ * its counters on `stream` first, so calls whose kernels overlap on the GPU (other
+ * streams, other host threads) race and give wrong results: issue them in one stream
+ * order.
  */
 int arc_fp8_fp4_gemm_noalloc(const uint8_t *A, const float *sfa, const uint8_t *Wp, const float *sfw,
                              uint16_t *C, int M, int N, int K, cudaStream_t stream);

@@ -210,6 +210,25 @@ def fp8fp4_out(x_bits, sfa, w_packed, sfw) -> np.ndarray:
     return a @ w.T
 
 
+# ------------------------------------------------------------ activation quantizer
+def int8_per_token_quant(x_bits: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """Per-token int8 quantisation of bf16 activations, in numpy float32 arithmetic.
+
+    The shape of the reference's per-token activation cast
+    (arc/testing/quant.py:30-48, per_token_cast_to_fp8: row amax over |x| in fp32,
+    clamped below at 1e-4, scale = amax / format max, codes = x / scale cast to the
+    format), restated for the int8 recipe: format max 127, the codes rounded half to
+    even and clipped to [-127, 127].
+      x_bits [M, K] uint16 (bf16 bits) -> (q [M, K] int8, sa [M] float32)
+    """
+    x = (np.ascontiguousarray(x_bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+    amax = np.maximum(np.abs(x).max(axis=1), np.float32(1e-4)).astype(np.float32)
+    sa = (amax / np.float32(127.0)).astype(np.float32)
+    q = np.rint(x / sa[:, None]).astype(np.float32)
+    q = np.clip(q, -127, 127).astype(np.int8)
+    return q, sa
+
+
 # ----------------------------------------------------------------------- parity metric
 def bf16_ulp(x: np.ndarray) -> np.ndarray:
     """Spacing of bf16 numbers at |x| (normal range; subnormals get the min spacing)."""

@@ -1,9 +1,9 @@
 """Generate the committed golden fixtures in tests/golden/.
 
 Run from the repository root in a container where the reference checkout is
-available (its path is given by ARC_REFERENCE, default /root/reference):
+available, with ARC_REFERENCE set to its path:
 
-    python tests/golden/make_golden.py
+    ARC_REFERENCE=<path of the reference checkout> python tests/golden/make_golden.py
 
 Fixtures:
 
@@ -41,8 +41,15 @@ sys.path[:0] = [str(ROOT / "arc-gemm_b200"), str(ROOT)]
 FP4_GRID = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], dtype=np.float32)
 
 
+def _reference_path() -> str:
+    ref = os.environ.get("ARC_REFERENCE")
+    if not ref:
+        raise SystemExit("set ARC_REFERENCE to the path of the reference checkout")
+    return ref
+
+
 def _reference():
-    ref = os.environ.get("ARC_REFERENCE", "/root/reference")
+    ref = _reference_path()
     if not Path(ref, "arc", "math.py").exists():
         raise SystemExit(f"reference checkout not found at {ref}")
     sys.path.insert(0, ref)
@@ -149,7 +156,7 @@ def main():
     # Drop the reference package from sys.modules so the local `arc` imports cleanly.
     for name in [m for m in sys.modules if m == "arc" or m.startswith("arc.")]:
         del sys.modules[name]
-    sys.path.remove(os.environ.get("ARC_REFERENCE", "/root/reference"))
+    sys.path.remove(_reference_path())
     a8w4_small()
     bf16_small()
     print("golden fixtures written to", HERE)
