@@ -18,6 +18,9 @@ ARC_ERR_CUDA = 3
 ARC_ERR_NO_DEVICE = 4
 ARC_ERR_DEVICE_TIMEOUT = 5
 
+# Bits of arc_device_status (arc-gemm_b200/csrc/sm100.cuh): which kind of wait timed out.
+STATUS_TIMEOUT_PEER = 1 << 6
+
 
 class ArcError(RuntimeError):
     """A nonzero arc_status_t from the native library."""
@@ -62,6 +65,7 @@ SIGNATURES = {
     "arc_fp8_fp4_gemm_noalloc": ([_P, _P, _P, _P, _P, _I, _I, _I, _P], _I),
     "arc_a8w4_gemm_gather": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
     "arc_peer_barrier": ([_P, _I, _I, _P], _I),
+    "arc_peer_barrier_ex": ([_P, _I, _I, ctypes.c_uint64, _P], _I),
     "arc_ipc_export": ([_P, _P, ctypes.POINTER(ctypes.c_uint64)], _I),
     "arc_ipc_open": ([_P, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)], _I),
     "arc_ipc_close": ([_P], _I),

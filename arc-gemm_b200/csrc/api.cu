@@ -327,7 +327,9 @@ uint32_t ceil_div(uint32_t a, uint32_t b) { return (a + b - 1) / b; }
 // A8W4 work decomposition
 // ---------------------------------------------------------------------------------
 constexpr uint32_t kDecodeMaxM = 32;
-constexpr uint32_t kDecodeLongG = 32;  // K-groups per tile from which persistent plans use 2 CTAs/SM
+// K-groups per tile from which a decode problem is long enough to be bound by HBM rather
+// than by the launch chain: its plans may use both CTA slots of an SM.
+constexpr uint32_t kDecodeLongG = 64;
 
 // Decode-sized problems (M <= 32) stream the weights once, in 128-row tiles. A plan is a
 // K split S in {1, 2, 4}: S > 1 runs one wave of S-CTA clusters that reduce on chip
@@ -360,18 +362,17 @@ int plan_a8w4(int M, int N, int K, int sms, int max_c2, int max_c4, arc_a8w4_pla
       plan->token_tile = static_cast<int>(bt);
       return ARC_OK;
     }
+    // Short problems keep one CTA per SM (the next launch's CTAs take the other slot);
+    // long ones (many K-groups per tile) may use both slots: twice the CTAs streaming.
+    const uint32_t slots = static_cast<uint32_t>(sms) * (G >= kDecodeLongG ? 2u : 1u);
     for (uint32_t S : {4u, 2u}) {
       const int cap = S == 2 ? max_c2 : max_c4;
-      if (S <= G && tiles * S <= static_cast<uint32_t>(sms) && tiles <= static_cast<uint32_t>(cap)) {
+      if (S <= G && tiles * S <= slots && tiles <= static_cast<uint32_t>(cap)) {
         decode_plan(bt, S, tiles * S, plan);
         return ARC_OK;
       }
     }
-    // Persistent tiles. A CTA keeps four 16 KiB weight stages in flight; problems long
-    // enough to be bound by HBM rather than by the launch chain (many K-groups per tile)
-    // run two CTAs per SM, twice the bytes in flight per SM.
-    const uint32_t cap = static_cast<uint32_t>(sms) * (G >= kDecodeLongG ? 2u : 1u);
-    decode_plan(bt, 1, tiles < cap ? tiles : cap, plan);
+    decode_plan(bt, 1, tiles < slots ? tiles : slots, plan);
     return ARC_OK;
   }
   const uint32_t bt = M <= 64 ? 64u : 128u;
@@ -691,8 +692,9 @@ int arc_a8w4_describe_plan(int M, int N, int K, int num_sms, arc_a8w4_plan_t* pl
   if (K % static_cast<int>(arcb::a8w4::kGroupK) != 0) {
     return fail(ARC_ERR_UNSUPPORTED, "arc_a8w4_describe_plan: K must be a multiple of 128");
   }
-  // Without a device: assume clusters of 2 and 4 tile the SMs completely.
-  return plan_a8w4(M, N, K, num_sms, num_sms / 2, num_sms / 4, plan);
+  // Without a device: two decode CTAs fit on an SM, and clusters of 2 and 4 tile the
+  // SMs completely.
+  return plan_a8w4(M, N, K, num_sms, num_sms, num_sms / 2, plan);
 }
 
 int arc_a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_t* sb,
@@ -846,7 +848,14 @@ int arc_ipc_close(void* base) {
 }
 
 int arc_peer_barrier(uint32_t* const* flags, int world, int rank, cudaStream_t stream) {
+  return arc_peer_barrier_ex(flags, world, rank, arcb::kWaitTimeoutNs, stream);
+}
+
+int arc_peer_barrier_ex(uint32_t* const* flags, int world, int rank, uint64_t timeout_ns, cudaStream_t stream) {
   g_last_error[0] = '\0';
+  if (timeout_ns == 0 || timeout_ns > arcb::kWaitTimeoutNs) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_peer_barrier_ex: timeout must be in (0, 2 s]");
+  }
   if (flags == nullptr || world < 1 || world > static_cast<int>(arcb::peer::kMaxPeers) || rank < 0 ||
       rank >= world) {
     return fail(ARC_ERR_INVALID_ARGUMENT, "arc_peer_barrier: bad flags / world (%d) / rank (%d)", world, rank);
@@ -860,10 +869,10 @@ int arc_peer_barrier(uint32_t* const* flags, int world, int rank, cudaStream_t s
   }
   b.world = static_cast<uint32_t>(world);
   b.rank = static_cast<uint32_t>(rank);
+  b.timeout_ns = timeout_ns;
   int dev = 0;
   if (int st = current_device(&dev)) return st;
-  arcb::peer::peer_barrier_kernel<<<1, 32, 0, stream>>>(b);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = launch_ex(arcb::peer::peer_barrier_kernel, b, 1, 32, 0, 1, stream);
   if (e != cudaSuccess) return cuda_fail(e, "peer_barrier_kernel launch");
   return ARC_OK;
 }
@@ -949,6 +958,10 @@ int a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_
     p.static_weights = (flags & ARC_A8W4_STATIC_WEIGHTS) ? 1u : 0u;
     p.sb_vec = (G % 8 == 0 && aligned16(sb)) ? 1u : 0u;
     const uint32_t grid = static_cast<uint32_t>(plan.grid);
+    // Stream mode when some CTA has more load stages than the ring holds.
+    const uint32_t ng_max = ceil_div(G, S);
+    const uint32_t items_max = S > 1 ? 1u : ceil_div(p.num_items, grid);
+    p.stream = items_max * ((ng_max + 1) / 2) > D::kWStages ? 1u : 0u;
     if (BT == 16) {
       e = launch_ex(D::gemm_a8w4_decode_kernel<16>, p, grid, D::kThreads, decode_smem_bytes<16>(), S, stream);
     } else {

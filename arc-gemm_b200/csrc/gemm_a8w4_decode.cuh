@@ -73,6 +73,11 @@ struct Params {
   uint32_t split;      // Wp in the pre-packed layout (a8w4::expand_piece)
   uint32_t static_weights;  // Wp and sb are not written by the preceding kernel
   uint32_t sb_vec;     // sb rows 16-byte aligned with G % 8 == 0: 8 scales per load
+  // Stream mode, for CTAs with more load stages than the ring holds: both groups of a
+  // stage are unpacked into TMEM (two stage slots of 64 columns), so a ring stage is free
+  // as soon as it has been read and the loads run ahead of the UMMAs. Otherwise (chunk
+  // mode) the second group stays in the ring stage, unpacked in place, until its UMMAs.
+  uint32_t stream;
   // Fused all-gather (peers > 0): every output tile is stored into each rank's output
   // through tm_peer[i], the [M][N] column window of rank i's gathered [M][world*N] output
   // that this rank owns (peer memory over NVLink; TMA stores only). tm_out is then unused.
@@ -104,6 +109,7 @@ struct alignas(1024) Smem {
   uint64_t w_full[kWStages];
   uint64_t w_empty[kWStages];                   // the stage's UMMAs retired
   uint64_t a_full[kWStages];                    // the stage is unpacked
+  uint64_t a_empty[2];                          // stream mode: a TMEM stage slot's UMMAs retired
   uint64_t t_full[C::kTStages];
   uint64_t t_empty[C::kTStages];
   uint64_t mma_done[C::kDStages];               // a stage's UMMAs retired
@@ -154,6 +160,14 @@ __device__ __forceinline__ bool warp_wait_poll(uint64_t* bar, uint32_t parity, v
   return __all_sync(0xffffffffu, ok);
 }
 
+// acc[c] = fma(float(P16[c]), s, acc[c]) for the BT int32 partials r[off .. off+BT)
+// (|16P| < 2^22, so the conversion is exact).
+template <uint32_t BT>
+__device__ __forceinline__ void accumulate(float (&acc)[BT], const uint32_t (&r)[32], uint32_t off, float s) {
+#pragma unroll
+  for (uint32_t c = 0; c < BT; ++c) acc[c] = fmaf(static_cast<float>(static_cast<int32_t>(r[off + c])), s, acc[c]);
+}
+
 // bf16 scale j (0..7) of an 8-scale window, as fp32.
 __device__ __forceinline__ float window_scale(const uint4& w, uint32_t j) {
   const uint32_t word = (j & 4u) ? ((j & 2u) ? w.w : w.z) : ((j & 2u) ? w.y : w.x);
@@ -182,9 +196,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     // operation with a long latency).
     for (uint32_t i = lane; i < kWStages; i += 32) {
       mbar_init(&s.w_full[i], 1);
-      mbar_init(&s.w_empty[i], 1);  // the stage's issuer commits
+      // Freed by the stage's issuer (chunk mode) or by the four unpack warps (stream mode).
+      mbar_init(&s.w_empty[i], p.stream ? 4 : 1);
       mbar_init(&s.a_full[i], 4);   // the four unpack warps
     }
+    for (uint32_t i = lane; i < 2; i += 32) mbar_init(&s.a_empty[i], 1);
     for (uint32_t i = lane; i < C::kTStages; i += 32) {
       mbar_init(&s.t_full[i], 1);
       mbar_init(&s.t_empty[i], 1);
@@ -285,12 +301,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       bool ok = true;
       for (uint32_t t = q; ok && t < ns; t += 2) {
         const uint32_t ts = t % C::kTStages, ws = t % kWStages, ds = t % C::kDStages;
+        // A slot of the stage: the ring slot (chunk mode) or one of two TMEM stage slots.
+        const uint32_t as = p.stream ? (t & 1u) : ws;
+        const uint32_t a_par = p.stream ? ((t >> 1) & 1u) : ((t / kWStages) & 1u);
         // The three tests are issued together (each costs ~200 cycles even when complete).
         const uint32_t t_t = mbar_test(&s.t_full[ts], (t / C::kTStages) & 1u);
-        const uint32_t t_a = mbar_test(&s.a_full[ws], (t / kWStages) & 1u);
+        const uint32_t t_a = mbar_test(&s.a_full[as], a_par);
         const uint32_t t_d = t < C::kDStages ? 1u : mbar_test(&s.tmem_empty[ds], ((t / C::kDStages) & 1u) ^ 1u);
         if ((t_t == 0u && !mbar_wait_poll(&s.t_full[ts], (t / C::kTStages) & 1u, abort, kStatusTimeoutMma)) ||
-            (t_a == 0u && !mbar_wait_poll(&s.a_full[ws], (t / kWStages) & 1u, abort, kStatusTimeoutMma)) ||
+            (t_a == 0u && !mbar_wait_poll(&s.a_full[as], a_par, abort, kStatusTimeoutMma)) ||
             (t_d == 0u &&
              !mbar_wait_poll(&s.tmem_empty[ds], ((t / C::kDStages) & 1u) ^ 1u, abort, kStatusTimeoutMma))) {
           ok = false;
@@ -299,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         tc_fence_after_sync();
         probe_mark(24 + (t & 7u));  // stage's waits passed
         const uint32_t d = tmem_base + C::kDBase + ds * 2u * BT;
-        const uint32_t a = tmem_base + ws * 32u;
+        const uint32_t a = tmem_base + as * (p.stream ? 64u : 32u);
         const uint64_t b = desc_advance(tdesc0, ts * C::kTokStage);
         // The two groups' K steps alternate, so consecutive UMMAs accumulate into
         // different TMEM columns and the tensor pipe never waits on the previous one.
@@ -309,10 +328,16 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (uint32_t j = 0; j < 4; ++j) {
           umma_s8_tmem_a(d, a + 8u * j, desc_advance(b, 32 * j), idesc, j > 0 ? 1u : 0u);
-          if (two) umma_s8(d + BT, desc_advance(w, 32 * j), desc_advance(b2, 32 * j), idesc, j > 0 ? 1u : 0u);
+          if (two) {
+            if (p.stream) {
+              umma_s8_tmem_a(d + BT, a + 32u + 8u * j, desc_advance(b2, 32 * j), idesc, j > 0 ? 1u : 0u);
+            } else {
+              umma_s8(d + BT, desc_advance(w, 32 * j), desc_advance(b2, 32 * j), idesc, j > 0 ? 1u : 0u);
+            }
+          }
         }
         umma_commit(&s.mma_done[ds]);
-        umma_commit(&s.w_empty[ws]);
+        umma_commit(p.stream ? &s.a_empty[as] : &s.w_empty[ws]);
         umma_commit(&s.t_empty[ts]);
         probe_mark(16 + (t & 15u));  // stage issued
       }
@@ -330,16 +355,21 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t lane_addr = ((warp - 4) * 32u) << 16;
     const uint32_t sw = nl & 7u;
     bool ok = true;
-    // With static weights the first kWStages stages are unpacked before the preceding
-    // grid is waited for; every later wait depends on the UMMAs, hence on the tokens.
+    // With static weights the stages that fit the A slots are unpacked before the
+    // preceding grid is waited for; every later wait depends on the UMMAs, hence on the
+    // tokens.
+    const uint32_t pre = p.stream ? 2u : kWStages;
     if (!p.static_weights) pdl_wait();
     for (uint32_t t = 0; ok && t < ns; ++t) {
-      if (p.static_weights && t == kWStages) pdl_wait();
+      if (p.static_weights && t == pre) pdl_wait();
       const uint32_t ws = t % kWStages;
-      if (!warp_wait(&s.w_full[ws], (t / kWStages) & 1u, abort, kStatusTimeoutUnpack)) {
+      const uint32_t as = p.stream ? (t & 1u) : ws;
+      if (!warp_wait(&s.w_full[ws], (t / kWStages) & 1u, abort, kStatusTimeoutUnpack) ||
+          (p.stream && t >= 2 && !warp_wait(&s.a_empty[as], ((t >> 1) & 1u) ^ 1u, abort, kStatusTimeoutUnpack))) {
         ok = false;
         break;
       }
+      if (p.stream) tc_fence_after_sync();  // the TMEM slot's previous UMMAs have retired
       uint8_t* row = s.wring[ws] + nl * (kGps * kPackedRow);
       uint4 x[8];
 #pragma unroll
@@ -360,24 +390,49 @@ __global__ void __launch_bounds__(kThreads, 2)
           v[8 * c + 6] = hi.z;
           v[8 * c + 7] = hi.w;
         }
-        tmem_st_32x32b_x16(tmem_base + lane_addr + ws * 32u + 16u * h, v);
+        tmem_st_32x32b_x16(tmem_base + lane_addr + as * (p.stream ? 64u : 32u) + 16u * h, v);
       }
       if (wk.has_second(t)) {
-        // K-major SW128: 16-byte chunk u (k = 16u .. 16u+15) of row nl at (u ^ (nl & 7)).
+        if (p.stream) {
+          // Second group: TMEM columns [64 * slot + 32, +32).
 #pragma unroll
-        for (uint32_t c = 0; c < 4; ++c) {
-          uint4 lo, hi;
-          expand_piece(x[4 + c], p.split, lo, hi);
-          *reinterpret_cast<uint4*>(row + (((2u * c) ^ sw) << 4)) = lo;
-          *reinterpret_cast<uint4*>(row + (((2u * c + 1u) ^ sw) << 4)) = hi;
+          for (uint32_t h = 0; h < 2; ++h) {
+            uint32_t v[16];
+#pragma unroll
+            for (uint32_t c = 0; c < 2; ++c) {
+              uint4 lo, hi;
+              expand_piece(x[4 + 2 * h + c], p.split, lo, hi);
+              v[8 * c + 0] = lo.x;
+              v[8 * c + 1] = lo.y;
+              v[8 * c + 2] = lo.z;
+              v[8 * c + 3] = lo.w;
+              v[8 * c + 4] = hi.x;
+              v[8 * c + 5] = hi.y;
+              v[8 * c + 6] = hi.z;
+              v[8 * c + 7] = hi.w;
+            }
+            tmem_st_32x32b_x16(tmem_base + lane_addr + as * 64u + 32u + 16u * h, v);
+          }
+        } else {
+          // K-major SW128: 16-byte chunk u (k = 16u .. 16u+15) of row nl at (u ^ (nl & 7)).
+#pragma unroll
+          for (uint32_t c = 0; c < 4; ++c) {
+            uint4 lo, hi;
+            expand_piece(x[4 + c], p.split, lo, hi);
+            *reinterpret_cast<uint4*>(row + (((2u * c) ^ sw) << 4)) = lo;
+            *reinterpret_cast<uint4*>(row + (((2u * c + 1u) ^ sw) << 4)) = hi;
+          }
+          fence_proxy_async_smem();
         }
-        fence_proxy_async_smem();
       }
       tmem_st_wait();
       tc_fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s.a_full[ws]);
-      if (warp == 4 && lane == 0 && t + 1 == (ns < kWStages ? ns : kWStages)) probe_mark(4);  // first ring unpacked
+      if (lane == 0) {
+        mbar_arrive(&s.a_full[as]);
+        if (p.stream) mbar_arrive(&s.w_empty[ws]);  // the stage has been read: reload it
+      }
+      if (warp == 4 && lane == 0 && t + 1 == (ns < pre ? ns : pre)) probe_mark(4);  // first A slots unpacked
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------------ epilogue warps
@@ -446,17 +501,10 @@ __global__ void __launch_bounds__(kThreads, 2)
           tc_fence_before_sync();
           __syncwarp();
           if (lane == 0) mbar_arrive(&s.tmem_empty[ds]);
-#pragma unroll
-          for (uint32_t c = 0; c < 16; ++c) acc[c] = fmaf(static_cast<float>(static_cast<int32_t>(r[c])), s0, acc[c]);
-          if (second) {
-#pragma unroll
-            for (uint32_t c = 0; c < 16; ++c) {
-              acc[c] = fmaf(static_cast<float>(static_cast<int32_t>(r[16 + c])), s1, acc[c]);
-            }
-          }
+          accumulate<16>(acc, r, 0, s0);
+          if (second) accumulate<16>(acc, r, 16, s1);
         } else {
-#pragma unroll
-          for (uint32_t c = 0; c < 32; ++c) acc[c] = fmaf(static_cast<float>(static_cast<int32_t>(r[c])), s0, acc[c]);
+          accumulate<32>(acc, r, 0, s0);
           if (p.partials != nullptr && n_valid) {
             const uint32_t g = wk.g0 + gi;
 #pragma unroll
@@ -471,12 +519,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           tc_fence_before_sync();
           __syncwarp();
           if (lane == 0) mbar_arrive(&s.tmem_empty[ds]);
-          if (second) {
-#pragma unroll
-            for (uint32_t c = 0; c < 32; ++c) {
-              acc[c] = fmaf(static_cast<float>(static_cast<int32_t>(r[c])), s1, acc[c]);
-            }
-          }
+          if (second) accumulate<32>(acc, r, 0, s1);
         }
         if (p.partials != nullptr && n_valid) {
           // r holds the second group's partials (BT=32), or both groups' (BT=16).

@@ -108,15 +108,22 @@ def load_peaks():
             "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
-def traffic_from_profiles(workload: str):
-    """DRAM bytes per launch from a committed ncu summary, if one exists."""
+def traffic_from_profiles(workload: str, kind: str = "a8w4", n_rank: int | None = None):
+    """DRAM bytes per launch from a committed ncu summary, if one exists. A record taken
+    at another number of weight columns (column sharding) is scaled to this rank's share
+    for A8W4, whose traffic is the weights'; other kinds report none then."""
     f = ROOT / "profiles" / f"traffic_{workload}.json"
-    if f.exists():
-        try:
-            return json.loads(f.read_text()).get("dram_bytes_per_launch")
-        except (ValueError, OSError):
-            return None
-    return None
+    if not f.exists():
+        return None
+    try:
+        rec = json.loads(f.read_text())
+    except (ValueError, OSError):
+        return None
+    val = rec.get("dram_bytes_per_launch")
+    n_rec = rec.get("N")
+    if val is None or n_rank is None or n_rec is None or n_rec == n_rank:
+        return val
+    return int(val * n_rank / n_rec) if kind == "a8w4" else None
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -477,7 +484,7 @@ def roofline(kind, M, n_rank, K, kernel_ms, peaks, name):
             unit = "TOPS" if kind == "a8w4" else "TFLOP/s"
             note = f"2 x bf16_tflops ({peaks['source']}): dense int8/fp8 = 2x dense bf16"
     return {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
-            "traffic": traffic_from_profiles(name), "peak_source": note,
+            "traffic": traffic_from_profiles(name, kind, n_rank), "peak_source": note,
             "algorithmic_per_launch": by if bound == "hbm" else ops,
             "algorithmic_unit": "bytes" if bound == "hbm" else "ops",
             "kernel": kernel_launched(kind, M, n_rank, K)}

@@ -179,6 +179,13 @@ int arc_a8w4_gemm_gather_ex(const int8_t *A, const float *sa, const uint8_t *Wp,
  */
 int arc_peer_barrier(uint32_t *const *flags, int world, int rank, cudaStream_t stream);
 
+/* arc_peer_barrier with the bound of its wait given in nanoseconds (0 < timeout_ns <= 2 s):
+ * a barrier whose peers have not announced within it sets the kStatusTimeoutPeer bit
+ * (1 << 6) of arc_device_status and returns. Where the reference would exit() on a failed
+ * CUDA call (arc/include/common.cuh:8-28), a missing peer is reported here. */
+int arc_peer_barrier_ex(uint32_t *const *flags, int world, int rank, uint64_t timeout_ns,
+                        cudaStream_t stream);
+
 /*
  * CUDA IPC for the buffers of a fused all-gather (no reference counterpart: the reference
  * is single-GPU). arc_ipc_export writes the ARC_IPC_HANDLE_BYTES-byte handle of the

@@ -103,6 +103,9 @@ def test_invalid_arguments_are_rejected_before_any_cuda_call(native_lib):
     # large N: persistent unsplit 128-row tiles
     (1, 28672, 8192, dict(split=0, token_tile=16, weight_rows=128, grid=224)),
     (16, 14336, 4096, dict(split=0, k_split=1, grid=112)),
+    # long K: splits use both CTA slots of an SM (two per SM, at most 296 CTAs)
+    (16, 14336, 8192, dict(split=1, k_split=2, grid=224)),
+    (16, 7168, 8192, dict(split=1, k_split=4, grid=224)),
     (32, 4096, 4096, dict(split=1, token_tile=32, k_split=4)),
     # K of one or two groups limits the split
     (16, 512, 128, dict(split=0, k_split=1, grid=4)),
@@ -119,9 +122,9 @@ def test_plans(native_lib, m, n, k, expect):
         assert plan["k_split"] in (1, 2, 4) and plan["k_split"] <= k // 128
         tiles = -(-n // 128)
         if plan["split"]:
-            assert plan["grid"] == tiles * plan["k_split"] <= 148
-        else:  # long tiles (>= 32 K-groups) run up to two CTAs per SM
-            assert plan["grid"] == min(tiles, 148 * (2 if k // 128 >= 32 else 1))
+            assert plan["grid"] == tiles * plan["k_split"] <= 148 * (2 if k // 128 >= 64 else 1)
+        else:  # long tiles (>= 64 K-groups) run up to two CTAs per SM
+            assert plan["grid"] == min(tiles, 148 * (2 if k // 128 >= 64 else 1))
         # weights stream in stages of two K-groups (a 128-byte box row) through 4 stages
         assert plan["groups_per_stage"] == 2 and plan["load_stages"] == 4
 

@@ -176,10 +176,13 @@ def test_a8w4_decode_decompositions(cuda_device, monkeypatch, plan):
     """Every decode decomposition is exact; forced per test. K split over 4- and 2-CTA
     clusters, persistent unsplit tiles, and persistent CTAs capped at 3 and 1 so that each
     walks several tiles (the A slots, load stages and accumulators carry over between
-    tiles). K = 384 and 640 give one-group load stages and uneven splits."""
+    tiles). K = 384 and 640 give one-group load stages and uneven splits; K = 8192 and the
+    capped grids give CTAs with more load stages than the ring holds (stream mode: both
+    groups of a stage unpacked into TMEM, ring stages refilled ahead of the UMMAs)."""
     monkeypatch.setenv("ARC_DECODE_PLAN", plan)
     S = int(plan.split(":")[1])
-    for m, n, k in ((16, 1000, 1024), (3, 512, 2048), (32, 256, 512), (16, 1000, 384), (7, 264, 640)):
+    for m, n, k in ((16, 1000, 1024), (3, 512, 2048), (32, 256, 512), (16, 1000, 384), (7, 264, 640),
+                    (16, 384, 8192)):
         for static in (False, True):
             (x, sa), (wp, sb) = generate_a8w4(m, n, k, seed=S + m + k)
             dev = cuda_device
