@@ -142,8 +142,16 @@ struct Walk {
   __device__ __forceinline__ uint32_t n0(const Params& p, uint32_t k) const {
     return (p.S > 1 ? blockIdx.x / p.S : blockIdx.x + k * gridDim.x) * kRows;
   }
-  // Stage t covers groups gi = 2*(t % spi) and gi + 1 (if gi + 1 < ng) of tile t / spi.
-  __device__ __forceinline__ bool has_second(uint32_t t) const { return 2u * (t % spi) + 1u < ng; }
+  // Stage t covers groups 2j and 2j + 1 (if 2j + 1 < ng) of tile k, with k = t / spi and
+  // j = t % spi. Loops keep (k, j) as a cursor and step it, instead of dividing.
+  __device__ __forceinline__ void advance(uint32_t& k, uint32_t& j, uint32_t step) const {
+    j += step;
+    while (j >= spi) {
+      j -= spi;
+      ++k;
+    }
+  }
+  __device__ __forceinline__ bool has_second(uint32_t j) const { return 2u * j + 1u < ng; }
 };
 
 // Every lane of the warp waits; the warp proceeds only if all of them succeeded,
@@ -160,12 +168,16 @@ __device__ __forceinline__ bool warp_wait_poll(uint64_t* bar, uint32_t parity, v
   return __all_sync(0xffffffffu, ok);
 }
 
-// acc[c] = fma(float(P16[c]), s, acc[c]) for the BT int32 partials r[off .. off+BT)
-// (|16P| < 2^22, so the conversion is exact).
+// acc[c] = fma(16P[c], s, acc[c]) for the BT int32 partials r[off .. off+BT). An int32 16P
+// (|16P| < 2^22) becomes a float with two full-rate operations instead of a conversion:
+// bits(16P) + bits(1.5 * 2^23) is the float 1.5 * 2^23 + 16P exactly, and subtracting
+// 1.5 * 2^23 leaves 16P exactly (the same value a conversion gives).
 template <uint32_t BT>
 __device__ __forceinline__ void accumulate(float (&acc)[BT], const uint32_t (&r)[32], uint32_t off, float s) {
 #pragma unroll
-  for (uint32_t c = 0; c < BT; ++c) acc[c] = fmaf(static_cast<float>(static_cast<int32_t>(r[off + c])), s, acc[c]);
+  for (uint32_t c = 0; c < BT; ++c) {
+    acc[c] = fmaf(__uint_as_float(r[off + c] + 0x4B400000u) - 12582912.0f, s, acc[c]);
+  }
 }
 
 // bf16 scale j (0..7) of an 8-scale window, as fp32.
@@ -241,6 +253,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // first kWStages are issued before the wait for the preceding grid.
     if (lane == 0) {
       uint32_t wi = 0, ti = 0;  // weight / token stages issued
+      uint32_t wk_k = 0, wk_j = 0, tk_j = 0;  // (tile, stage) of the next weight / token stage
       bool ok = true;
       auto issue_w = [&](uint32_t t) -> bool {
         const uint32_t slot = t % kWStages;
@@ -249,8 +262,9 @@ __global__ void __launch_bounds__(kThreads, 2)
           return false;
         }
         mbar_arrive_expect_tx(&s.w_full[slot], kWStageBytes);
-        tma_load_2d(&p.tm_wp, &s.w_full[slot], s.wring[slot], int32_t((wk.g0 + 2u * (t % wk.spi)) * kPackedRow),
-                    int32_t(wk.n0(p, t / wk.spi)), kCacheEvictFirst);
+        tma_load_2d(&p.tm_wp, &s.w_full[slot], s.wring[slot], int32_t((wk.g0 + 2u * wk_j) * kPackedRow),
+                    int32_t(wk.n0(p, wk_k)), kCacheEvictFirst);
+        wk.advance(wk_k, wk_j, 1);
         return true;
       };
       if (p.static_weights) {
@@ -270,8 +284,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           break;
         }
         mbar_arrive_expect_tx(&s.t_full[slot], C::kTokStage);
-        tma_load_3d(&p.tm_tok, &s.t_full[slot], s.tring[slot], 0, 0, int32_t(wk.g0 + 2u * (t % wk.spi)),
-                    kCacheEvictLast);
+        tma_load_3d(&p.tm_tok, &s.t_full[slot], s.tring[slot], 0, 0, int32_t(wk.g0 + 2u * tk_j), kCacheEvictLast);
+        if (++tk_j == wk.spi) tk_j = 0;
         ++ti;
       }
       // Every load issued lands before the CTA may exit.
@@ -299,7 +313,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint64_t tdesc0 = make_sw128_kmajor_desc(s.tring);
       const uint64_t wdesc0 = make_sw128_kmajor_desc(s.wring);
       bool ok = true;
-      for (uint32_t t = q; ok && t < ns; t += 2) {
+      uint32_t ck = 0, cj = 0;  // (tile, stage) of stage t
+      wk.advance(ck, cj, q);
+      for (uint32_t t = q; ok && t < ns; t += 2, wk.advance(ck, cj, 2)) {
         const uint32_t ts = t % C::kTStages, ws = t % kWStages, ds = t % C::kDStages;
         // A slot of the stage: the ring slot (chunk mode) or one of two TMEM stage slots.
         const uint32_t as = p.stream ? (t & 1u) : ws;
@@ -322,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint64_t b = desc_advance(tdesc0, ts * C::kTokStage);
         // The two groups' K steps alternate, so consecutive UMMAs accumulate into
         // different TMEM columns and the tensor pipe never waits on the previous one.
-        const bool two = wk.has_second(t);
+        const bool two = wk.has_second(cj);
         const uint64_t w = desc_advance(wdesc0, ws * kWStageBytes);
         const uint64_t b2 = desc_advance(b, C::kTokTile);
 #pragma unroll
@@ -360,7 +376,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     // tokens.
     const uint32_t pre = p.stream ? 2u : kWStages;
     if (!p.static_weights) pdl_wait();
-    for (uint32_t t = 0; ok && t < ns; ++t) {
+    uint32_t uj = 0;  // stage of stage t within its tile
+    for (uint32_t t = 0; ok && t < ns; ++t, uj = (uj + 1 == wk.spi) ? 0u : uj + 1) {
       if (p.static_weights && t == pre) pdl_wait();
       const uint32_t ws = t % kWStages;
       const uint32_t as = p.stream ? (t & 1u) : ws;
@@ -392,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         tmem_st_32x32b_x16(tmem_base + lane_addr + as * (p.stream ? 64u : 32u) + 16u * h, v);
       }
-      if (wk.has_second(t)) {
+      if (wk.has_second(uj)) {
         if (p.stream) {
           // Second group: TMEM columns [64 * slot + 32, +32).
 #pragma unroll
@@ -471,8 +488,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     float acc[BT];
 #pragma unroll
     for (uint32_t j = 0; j < BT; ++j) acc[j] = 0.f;
-    for (uint32_t t = 0; t < ns; ++t) {
-      const uint32_t k = t / wk.spi, gi = 2u * (t % wk.spi);
+    uint32_t k = 0, ej = 0;  // (tile, stage) of stage t
+    for (uint32_t t = 0; t < ns; ++t, wk.advance(k, ej, 1)) {
+      const uint32_t gi = 2u * ej;
       const bool second = gi + 1u < wk.ng;
       if (gi == 0 && k > 0) {  // next tile of a persistent CTA
         n = wk.n0(p, k) + nl;
