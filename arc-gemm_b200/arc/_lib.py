@@ -73,6 +73,7 @@ SIGNATURES = {
     "arc_a8w4_gemm_prepacked": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _P], _I),
     "arc_a8w4_gemm_ex": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_uint, _P, _P], _I),
     "arc_a8w4_gemm_gather_ex": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, ctypes.c_uint, _P], _I),
+    "arc_a8w4_gemm_gather_sync": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, ctypes.c_uint, _P], _I),
 }
 
 # Flags of arc_a8w4_gemm_ex / arc_a8w4_gemm_gather_ex (include/arc_b200.h).

@@ -542,7 +542,7 @@ int fp8fp4_gemm(const uint8_t* A, const float* sfa, const uint8_t* Wp, const flo
                 int M, int N, int K, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 int a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_t* sb, uint16_t* C, int M,
               int N, int K, int group, cudaStream_t stream, int32_t* partials_dbg, uint16_t* const* outs,
-              int world, int rank, uint32_t flags);
+              int world, int rank, uint32_t flags, uint32_t* const* bar_flags = nullptr);
 
 }  // namespace
 
@@ -792,6 +792,41 @@ int arc_a8w4_gemm_gather(const int8_t* A, const float* sa, const uint8_t* Wp, co
   return arc_a8w4_gemm_gather_ex(A, sa, Wp, sb, outs, world, rank, M, N, K, 0u, stream);
 }
 
+int arc_a8w4_gemm_gather_sync(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_t* sb,
+                              uint16_t* const* outs, uint32_t* const* bar_flags, int world, int rank, int M,
+                              int N, int K, unsigned flags, cudaStream_t stream) {
+  g_last_error[0] = '\0';
+  if (bar_flags == nullptr || world < 1 || world > static_cast<int>(arcb::peer::kMaxPeers)) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_a8w4_gemm_gather_sync: bad flags / world (%d)", world);
+  }
+  for (int i = 0; i < world; ++i) {
+    if (bar_flags[i] == nullptr || (reinterpret_cast<uintptr_t>(bar_flags[i]) & 3u)) {
+      return fail(ARC_ERR_INVALID_ARGUMENT, "arc_a8w4_gemm_gather_sync: flag array %d is null or misaligned", i);
+    }
+  }
+  if (flags & ~ARC_A8W4_STATIC_WEIGHTS) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_a8w4_gemm_gather_sync: unsupported flags 0x%x", flags);
+  }
+  if (outs == nullptr || rank < 0 || rank >= world) {
+    return fail(ARC_ERR_INVALID_ARGUMENT, "arc_a8w4_gemm_gather_sync: bad outs / rank (%d)", rank);
+  }
+  for (int i = 0; i < world; ++i) {
+    if (outs[i] == nullptr || !aligned16(outs[i])) {
+      return fail(ARC_ERR_INVALID_ARGUMENT, "arc_a8w4_gemm_gather_sync: output %d is null or not 16-byte aligned", i);
+    }
+  }
+  if (M <= 0 || M > static_cast<int>(kDecodeMaxM)) {
+    return fail(ARC_ERR_UNSUPPORTED,
+                "arc_a8w4_gemm_gather_sync: the fused all-gather covers decode batches (1 <= M <= %u, got %d)",
+                kDecodeMaxM, M);
+  }
+  if (N <= 0 || N % 8 != 0) {
+    return fail(ARC_ERR_UNSUPPORTED, "arc_a8w4_gemm_gather_sync: N (%d) must be a positive multiple of 8", N);
+  }
+  return a8w4_gemm(A, sa, Wp, sb, outs[rank] + size_t(rank) * N, M, N, K, 128, stream, nullptr, outs, world,
+                   rank, flags, bar_flags);
+}
+
 int arc_ipc_export(const void* ptr, void* handle, uint64_t* offset) {
   g_last_error[0] = '\0';
   if (ptr == nullptr || handle == nullptr || offset == nullptr) {
@@ -883,7 +918,7 @@ namespace {
 
 int a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_t* sb, uint16_t* C, int M,
               int N, int K, int group, cudaStream_t stream, int32_t* partials_dbg, uint16_t* const* outs,
-              int world, int rank, uint32_t flags) {
+              int world, int rank, uint32_t flags, uint32_t* const* bar_flags) {
   if (A == nullptr || sa == nullptr || Wp == nullptr || sb == nullptr || C == nullptr) {
     return fail(ARC_ERR_INVALID_ARGUMENT, "arc_a8w4_gemm: null pointer");
   }
@@ -943,6 +978,14 @@ int a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_
         }
       }
       p.peers = static_cast<uint32_t>(world);
+    }
+    p.bar_world = 0;
+    p.bar_rank = 0;
+    p.bar_timeout_ns = arcb::kWaitTimeoutNs;
+    if (bar_flags != nullptr) {
+      for (int i = 0; i < world; ++i) p.bar_flags[i] = bar_flags[i];
+      p.bar_world = static_cast<uint32_t>(world);
+      p.bar_rank = static_cast<uint32_t>(rank);
     }
     p.sa = sa;
     p.sb = sb;

@@ -83,6 +83,13 @@ struct Params {
   // that this rank owns (peer memory over NVLink; TMA stores only). tm_out is then unused.
   uint32_t peers;
   CUtensorMap tm_peer[kMaxPeers];
+  // Barrier of the fused all-gather folded into the kernel (bar_world > 0): bar_flags[i]
+  // is rank i's flag array (the layout of peer_barrier.cuh plus word world + 1, this
+  // rank's count of CTAs done). The last CTA to finish runs the barrier, so one launch
+  // per step both gathers and synchronises.
+  uint32_t* bar_flags[kMaxPeers];
+  uint32_t bar_world, bar_rank;
+  uint64_t bar_timeout_ns;
 };
 
 template <uint32_t BT>
@@ -635,7 +642,52 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     // The stores must have read their shared-memory tile before the CTA exits; their
     // global writes complete with the grid.
-    if (et == 0) tma_store_wait_read<0>();
+    if (et == 0) {
+      if (p.bar_world > 0) {
+        tma_store_wait_all<0>();  // every store (into every rank's output) performed
+      } else {
+        tma_store_wait_read<0>();
+      }
+    }
+    if (p.bar_world > 0 && qw == 0) {
+      // Folded barrier: the CTA that completes the count announces this rank's next epoch
+      // in every rank's flags and waits for every rank's (bounded), as peer_barrier.cuh
+      // does in a launch of its own.
+      const uint32_t world = p.bar_world;
+      uint32_t* counter = p.bar_flags[p.bar_rank] + world + 1;
+      uint32_t last = 0;
+      if (lane == 0) {
+        __threadfence_system();  // this CTA's peer stores before its count
+        last = atomicAdd(counter, 1u) + 1u == gridDim.x ? 1u : 0u;
+        if (last) {
+          *counter = 0u;           // ready for the next launch
+          __threadfence_system();  // every CTA's stores before the announcement
+        }
+      }
+      if (__shfl_sync(0xffffffffu, last, 0)) {
+        uint32_t* epochs = p.bar_flags[p.bar_rank] + world;
+        const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(epochs) + 1u;
+        if (lane < world) {
+          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.bar_flags[lane] + p.bar_rank), "r"(epoch)
+                       : "memory");
+          const uint32_t* f = p.bar_flags[p.bar_rank] + lane;
+          const uint64_t start = globaltimer_ns();
+#pragma unroll 1
+          for (uint32_t it = 0;; ++it) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+            if (static_cast<int32_t>(v - epoch) >= 0) break;
+            if ((it & 63u) == 63u && globaltimer_ns() - start > p.bar_timeout_ns) {
+              atomicOr(&g_arc_status, kStatusTimeoutPeer);
+              break;
+            }
+            __nanosleep(64);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) *epochs = epoch;
+      }
+    }
   }
 
   if (p.S > 1) {

@@ -161,6 +161,20 @@ int arc_a8w4_gemm_gather(const int8_t *A, const float *sa, const uint8_t *Wp, co
                          uint16_t *const *outs, int world, int rank, int M, int N, int K,
                          cudaStream_t stream);
 
+/*
+ * The fused all-gather GEMM and its barrier in ONE launch (no reference counterpart: the
+ * reference is single-GPU; the call shape is still tests/a8w4.py:48's, per rank). Same as
+ * arc_a8w4_gemm_gather_ex followed by arc_peer_barrier on the same flag arrays, except that
+ * the kernel's last CTA to finish runs the barrier, so the step costs one launch. flags[i]
+ * is rank i's flag array of world + 2 uint32 words, zeroed once: the world epochs and the
+ * barrier count of arc_peer_barrier, then a count of finished CTAs that the kernel leaves
+ * at zero. The wait for the peers gives up after 2 s and reports kStatusTimeoutPeer through
+ * arc_device_status. Every rank must make the same sequence of calls.
+ */
+int arc_a8w4_gemm_gather_sync(const int8_t *A, const float *sa, const uint8_t *Wp, const uint16_t *sb,
+                              uint16_t *const *outs, uint32_t *const *flags, int world, int rank, int M,
+                              int N, int K, unsigned gemm_flags, cudaStream_t stream);
+
 /* arc_a8w4_gemm_gather with the flags of arc_a8w4_gemm_ex (ARC_A8W4_STATIC_WEIGHTS; the
  * fused gather takes weights in the reference packing only). */
 int arc_a8w4_gemm_gather_ex(const int8_t *A, const float *sa, const uint8_t *Wp, const uint16_t *sb,

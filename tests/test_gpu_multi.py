@@ -87,7 +87,7 @@ def test_two_gpu_sharded_gemm_with_all_gather(m, n, k):
     assert all(p.exitcode == 0 for p in procs)
 
 
-def _fused_worker(rank, world, port, m, n, k, result_q):
+def _fused_worker(rank, world, port, m, n, k, result_q, one_launch=True):
     """Each rank: its column block through the GEMM with the fused all-gather, twice in a
     row (two barrier epochs). The gathered output must match the CPU oracle on sampled
     columns of every rank's block (within 2 bf16 ulps) and equal the NCCL all-gather of
@@ -117,7 +117,7 @@ def _fused_worker(rank, world, port, m, n, k, result_q):
     dist.init_process_group("nccl", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60), device_id=dev)
     try:
-        fg = par.FusedGather(m, n, device=dev)
+        fg = par.FusedGather(m, n, device=dev, one_launch=one_launch)
         ok = True
         for seed in (5, 6):
             (x, sa), (wp, sb) = generate_a8w4(m, n, k, seed=seed)
@@ -154,15 +154,18 @@ def _fused_worker(rank, world, port, m, n, k, result_q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("one_launch", [True, False])
 @pytest.mark.parametrize("m,n,k", [(16, 4096, 4096), (5, 1040, 1024)])
-def test_two_gpu_fused_all_gather(m, n, k):
+def test_two_gpu_fused_all_gather(m, n, k, one_launch):
+    """The barrier folded into the GEMM's last CTA (one launch per step) and the separate
+    barrier kernel give the same, oracle-checked output."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, m, n, k, q)) for r in range(world)]
+    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, m, n, k, q, one_launch)) for r in range(world)]
     for p in procs:
         p.start()
     try:
