@@ -590,7 +590,7 @@ class Runner:
             "timing": {
                 "l2": (f"{n_sets} copies of the inputs at distinct addresses "
                        f"({n_sets * in_bytes / 1e6:.0f} MB) > L2") if flush is None
-                      else "L2 flushed (512 MB write) before every timed step, outside its events",
+                      else f"L2 flushed ({2 * L2_BYTES >> 20} MiB write) before every timed step, outside its events",
                 "launch": (f"K steps ({launches} launch(es) each) in one CUDA graph" if use_graph
                            else "eager launches"),
                 "static_weights": kind == "a8w4",
