@@ -214,6 +214,17 @@ int init_device(int dev) {
     if (e == cudaSuccess) {
       e = allow_smem(arcb::a8w4dec::gemm_a8w4_decode_kernel<32>, decode_smem_bytes<32>());
     }
+    // The decode kernels move registers between warpgroups as well (64 per thread at
+    // launch, two CTAs per SM).
+    for (int v = 0; v < 2 && e == cudaSuccess; ++v) {
+      cudaFuncAttributes fa;
+      e = v == 0 ? cudaFuncGetAttributes(&fa, arcb::a8w4dec::gemm_a8w4_decode_kernel<16>)
+                 : cudaFuncGetAttributes(&fa, arcb::a8w4dec::gemm_a8w4_decode_kernel<32>);
+      if (e == cudaSuccess && fa.numRegs != static_cast<int>(arcb::a8w4dec::kLaunchRegs)) {
+        st.status = fail(ARC_ERR_UNSUPPORTED, "gemm_a8w4_decode_kernel was compiled with an unexpected register count");
+        return;
+      }
+    }
     if (e == cudaSuccess) {
       e = allow_smem(arcb::fp8fp4::gemm_fp8fp4_kernel<1>, sizeof(arcb::fp8fp4::Smem<1>) + 1024);
     }

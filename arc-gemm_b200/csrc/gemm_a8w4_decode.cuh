@@ -32,9 +32,12 @@
 //   TMEM lane = one output column), scale them by sb[n,g] and accumulate in fp32
 //   registers. Every hand-off between roles is paid once per stage, not per group.
 //
-// Roles (384 threads): warp 0 TMA producer, warps 1 and 3 UMMA issuers (even / odd
-// stages), warp 2 TMEM allocator, warps 4-7 unpack, warps 8-11 epilogue (warps 4+q and
-// 8+q own TMEM lanes 32q..32q+31).
+// Roles (512 threads): warp 0 TMA producer, warps 1 and 3 UMMA issuers (even / odd
+// stages), warp 2 TMEM allocator, warps 4-7 and 12-15 unpack (even / odd stages: a
+// stage's unpack is mostly latency, ~0.5 us per 16 KiB), warps 8-11 epilogue (warps
+// 4+q, 12+q and 8+q own TMEM lanes 32q..32q+31). Registers (setmaxnreg): 64 per thread
+// at launch (two CTAs per SM), the producer / issuer / allocator warpgroup drops to 40,
+// the epilogue rises to 80 (BT=16) or 88 (BT=32).
 //
 // Every wait is bounded (sm100.cuh: mbar_wait); a timeout sets a status bit, lets the
 // CTA's roles leave their loops and still pass every barrier they share.
@@ -51,7 +54,13 @@ using a8w4::kGroupK;
 using a8w4::kPackedRow;
 using a8w4::kRows;
 
-constexpr uint32_t kThreads = 384;
+constexpr uint32_t kThreads = 512;
+constexpr uint32_t kLaunchRegs = 64;  // 2 CTAs per SM
+constexpr uint32_t kRegsCtl = 40, kRegsUnpack = 64;
+// The epilogue's share: its BT running sums plus one stage's 32 partials and the scales.
+template <uint32_t BT>
+__host__ __device__ constexpr uint32_t regs_epi() { return BT == 16 ? 80u : 88u; }
+static_assert(128 * (kRegsCtl + 2 * kRegsUnpack + regs_epi<32>()) <= kThreads * kLaunchRegs, "register shares");
 constexpr uint32_t kTmemCols = 256;   // half an SM's TMEM: two CTAs share one SM
 constexpr uint32_t kGps = 2;          // K-groups per load stage (one 128-byte box row)
 constexpr uint32_t kWStageBytes = kRows * kGps * kPackedRow;  // 16 KiB of packed weights
@@ -125,7 +134,27 @@ struct alignas(1024) Smem {
   uint64_t recv_full;                           // peers' partials landed (S > 1)
   uint32_t tmem_base;
   uint32_t abort;
+#if defined(ARC_PROBE)
+  unsigned long long stamps[kProbeSlots];  // probe build: this CTA's stamps, copied out at teardown
+#endif
 };
+
+// Probe stamp (probe build only): %clock64 into shared memory, a few cycles, so that the
+// stamps barely move the pipeline they time. The CTA copies them to the attached probe
+// buffer when it ends (sm100.cuh: g_arc_probe, one row of kProbeSlots per CTA). Stamps
+// of different warps may come from different SM sub-partitions' counters: compare a
+// warp's stamps with its own.
+template <uint32_t BT>
+__device__ __forceinline__ void stamp(Smem<BT>& s, uint32_t slot) {
+#if defined(ARC_PROBE)
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(t));
+  if (slot < kProbeSlots) s.stamps[slot] = t;
+#else
+  (void)s;
+  (void)slot;
+#endif
+}
 
 // The sequence of load stages one CTA works through: `items` weight tiles of `ng`
 // K-groups each (one tile for S > 1), in stages of two consecutive groups of one tile
@@ -203,7 +232,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t lane = threadIdx.x & 31u;
   volatile uint32_t* abort = &s.abort;
 
-  if (threadIdx.x == 0) probe_mark(0);  // kernel entry
+#if defined(ARC_PROBE)
+  if (threadIdx.x == 0) {
+    for (uint32_t i = 0; i < kProbeSlots; ++i) s.stamps[i] = 0ull;
+  }
+#endif
+  if (threadIdx.x == 0) stamp(s, 0);  // kernel entry
   pdl_launch_dependents();
   if (warp == 0) {
     if (lane == 0) {
@@ -217,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&s.w_full[i], 1);
       // Freed by the stage's issuer (chunk mode) or by the four unpack warps (stream mode).
       mbar_init(&s.w_empty[i], p.stream ? 4 : 1);
-      mbar_init(&s.a_full[i], 4);   // the four unpack warps
+      mbar_init(&s.a_full[i], 4);   // the four warps of the stage's unpack warpgroup
     }
     for (uint32_t i = lane; i < 2; i += 32) mbar_init(&s.a_empty[i], 1);
     for (uint32_t i = lane; i < C::kTStages; i += 32) {
@@ -249,13 +283,16 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after_sync();
   if (p.S > 1) cluster_sync_all();  // every CTA's barriers exist before any exchange
-  if (threadIdx.x == 0) probe_mark(1);  // prologue done
+  if (threadIdx.x == 0) stamp(s, 1);  // prologue done
   const uint32_t tmem_base = s.tmem_base;
   const Walk wk(p);
   const uint32_t ns = wk.stages();
 
+  // Register moves sit inside each role's branch, so that the compiler gives every
+  // role's code the budget of that role.
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
+    regs_release<kRegsCtl>();
     // Weight stages run up to kWStages ahead of token stages; with static weights the
     // first kWStages are issued before the wait for the preceding grid.
     if (lane == 0) {
@@ -276,11 +313,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       };
       if (p.static_weights) {
         while (ok && wi < ns && wi < kWStages) ok = issue_w(wi++);
-        probe_mark(2);  // weights issued ahead of the wait
+        stamp(s, 2);  // weights issued ahead of the wait
       }
       // Tokens (and, without static_weights, everything) only after the preceding grid.
       pdl_wait();
-      probe_mark(3);  // preceding grid complete
+      stamp(s, 3);  // preceding grid complete
       for (uint32_t t = 0; ok && t < ns; ++t) {
         while (ok && wi < ns && wi < t + kWStages) ok = issue_w(wi++);
         if (!ok) break;
@@ -302,10 +339,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (uint32_t t = ti - (ti < C::kTStages ? ti : C::kTStages); t < ti; ++t) {
         mbar_drain(&s.t_full[t % C::kTStages], (t / C::kTStages) & 1u);
       }
-      probe_mark(10);  // producer drained
+      stamp(s, 10);  // producer drained
     }
   } else if (warp == 1 || warp == 3) {
     // ------------------------------------------------------------ UMMA issuers
+    regs_release<kRegsCtl>();
     // Issuer q takes the stages t with t % 2 == q. A stage: four K=32 UMMAs of its first
     // group (A from TMEM) and four of its second (A from the unpacked shared-memory
     // stage), B from the stage's token tiles, into the accumulator pair of slot
@@ -339,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           break;
         }
         tc_fence_after_sync();
-        probe_mark(24 + (t & 7u));  // stage's waits passed
+        stamp(s, 24 + (t & 7u));  // stage's waits passed
         const uint32_t d = tmem_base + C::kDBase + ds * 2u * BT;
         const uint32_t a = tmem_base + as * (p.stream ? 64u : 32u);
         const uint64_t b = desc_advance(tdesc0, ts * C::kTokStage);
@@ -362,30 +400,36 @@ __global__ void __launch_bounds__(kThreads, 2)
         umma_commit(&s.mma_done[ds]);
         umma_commit(p.stream ? &s.a_empty[as] : &s.w_empty[ws]);
         umma_commit(&s.t_empty[ts]);
-        probe_mark(16 + (t & 15u));  // stage issued
+        stamp(s, 16 + (t & 15u));  // stage issued
       }
       umma_commit(&s.drain);
       mbar_drain(&s.drain, 0);
-      probe_mark(11 + q);  // every UMMA of this issuer retired
+      stamp(s, 11 + q);  // every UMMA of this issuer retired
     }
-  } else if (warp >= 4 && warp < 8) {
+  } else if ((warp >= 4 && warp < 8) || warp >= 12) {
     // ------------------------------------------------------------ unpack warps
     // Thread = row nl of the stage (TMEM lane nl). The row's 128 packed bytes (two
     // groups, 16-byte chunks placed by the 128-byte swizzle) go to registers; the first
     // group's 128 int8 codes to TMEM columns [32 * slot, +32), the second's back into the
     // row's 128 bytes in the K-major SW128 layout.
-    const uint32_t nl = (warp - 4) * 32 + lane;
-    const uint32_t lane_addr = ((warp - 4) * 32u) << 16;
+    const uint32_t nl = (warp & 3u) * 32 + lane;
+    const uint32_t lane_addr = ((warp & 3u) * 32u) << 16;
     const uint32_t sw = nl & 7u;
+    const uint32_t ug = warp >= 12 ? 1u : 0u;  // unpack warpgroup: stages t with t % 2 == ug
     bool ok = true;
     // With static weights the stages that fit the A slots are unpacked before the
     // preceding grid is waited for; every later wait depends on the UMMAs, hence on the
     // tokens.
     const uint32_t pre = p.stream ? 2u : kWStages;
-    if (!p.static_weights) pdl_wait();
-    uint32_t uj = 0;  // stage of stage t within its tile
-    for (uint32_t t = 0; ok && t < ns; ++t, uj = (uj + 1 == wk.spi) ? 0u : uj + 1) {
-      if (p.static_weights && t == pre) pdl_wait();
+    bool waited = !p.static_weights;
+    if (waited) pdl_wait();
+    uint32_t uk = 0, uj = 0;  // (tile, stage) of stage t
+    wk.advance(uk, uj, ug);
+    for (uint32_t t = ug; ok && t < ns; t += 2, wk.advance(uk, uj, 2)) {
+      if (!waited && t >= pre) {
+        pdl_wait();
+        waited = true;
+      }
       const uint32_t ws = t % kWStages;
       const uint32_t as = p.stream ? (t & 1u) : ws;
       if (!warp_wait(&s.w_full[ws], (t / kWStages) & 1u, abort, kStatusTimeoutUnpack) ||
@@ -456,10 +500,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         mbar_arrive(&s.a_full[as]);
         if (p.stream) mbar_arrive(&s.w_empty[ws]);  // the stage has been read: reload it
       }
-      if (warp == 4 && lane == 0 && t + 1 == (ns < pre ? ns : pre)) probe_mark(4);  // first A slots unpacked
+      if ((warp & 7u) == 4u && lane == 0 && t + 2 >= (ns < pre ? ns : pre) && t < pre) stamp(s, 4);  // pre-wait stages unpacked
     }
-  } else if (warp >= 8) {
+  } else if (warp >= 8 && warp < 12) {
     // ------------------------------------------------------------ epilogue warps
+    regs_claim<regs_epi<BT>()>();
     const uint32_t qw = warp - 8;
     const uint32_t et = threadIdx.x - kEpiThread0;  // 0..127
     const uint32_t nl = qw * 32 + lane;             // row of the tile = TMEM lane
@@ -560,7 +605,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
           }
         }
-        if (qw == 0 && lane == 0) probe_mark(48 + (t & 15u));  // stage accumulated
+        if (qw == 0 && lane == 0) stamp(s, 48 + (t & 15u));  // stage accumulated
       }
       if (gi + 2u < wk.ng) continue;
 
@@ -602,7 +647,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         fence_proxy_async_smem();
         named_barrier_sync(1, 128);
         if (et == 0 && *abort == 0u) {
-          probe_mark(5);  // partials staged
+          stamp(s, 5);  // partials staged
           for (uint32_t o = 0; o < p.S; ++o) {
             if (o == rank) continue;
             bulk_copy_to_peer(map_to_rank(s.recv + rank * rows_per * BT, o), send + o * rows_per * BT,
@@ -610,7 +655,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
         }
         const bool got = warp_wait_poll(&s.recv_full, 0, abort, kStatusTimeoutEpilogue);
-        if (et == 0) probe_mark(6);  // peer partials landed
+        if (et == 0) stamp(s, 6);  // peer partials landed
         if (got) {
           const float sa_mine = __shfl_sync(0xffffffffu, sa_lane, lane % BT);  // token et % BT
           const float* own = send + rank * rows_per * BT;
@@ -623,10 +668,10 @@ __global__ void __launch_bounds__(kThreads, 2)
             tile[c * rows_per + rr] = __bfloat16_as_ushort(__float2bfloat16_rn(sum * sa_mine));
           }
         }
-        if (et == 0) probe_mark(8);  // owned slice summed
+        if (et == 0) stamp(s, 8);  // owned slice summed
         fence_proxy_async_smem();
         named_barrier_sync(1, 128);
-        if (et == 0) probe_mark(9);  // tile complete
+        if (et == 0) stamp(s, 9);  // tile complete
         if (et == 0 && *abort == 0u) {
           if (p.peers == 0) {
             tma_store_2d(&p.tm_out, tile, int32_t(n0 + rank * rows_per), 0);
@@ -636,7 +681,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
           }
           tma_store_commit();
-          probe_mark(7);  // output store issued
+          stamp(s, 7);  // output store issued
         }
       }
     }
@@ -688,6 +733,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (lane == 0) *epochs = epoch;
       }
     }
+  } else {
+    regs_release<kRegsCtl>();  // warp 2 (TMEM allocator) shares the producer's warpgroup
   }
 
   if (p.S > 1) {
@@ -698,12 +745,19 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncwarp();
     cluster_arrive_relaxed();
     cluster_wait();
-    if (threadIdx.x == 0) probe_mark(14);  // end-of-kernel cluster barrier passed
+    if (threadIdx.x == 0) stamp(s, 14);  // end-of-kernel cluster barrier passed
   }
 
   tc_fence_before_sync();
   __syncthreads();
-  if (threadIdx.x == 0) probe_mark(15);  // teardown
+  if (threadIdx.x == 0) stamp(s, 15);  // teardown
+#if defined(ARC_PROBE)
+  if (warp < 2) {
+    named_barrier_sync(3, 64);
+    unsigned long long* buf = g_arc_probe;
+    if (buf != nullptr) buf[blockIdx.x * kProbeSlots + threadIdx.x] = s.stamps[threadIdx.x];
+  }
+#endif
   if (warp == 2) {
     tc_fence_after_sync();
     tmem_dealloc(tmem_base, kTmemCols);
