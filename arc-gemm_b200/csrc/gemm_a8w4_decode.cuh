@@ -495,6 +495,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       tmem_st_wait();
       tc_fence_before_sync();
+      // Stream mode frees the ring stage for a TMA reload (async proxy): order this
+      // warp's generic reads of it first.
+      if (p.stream) fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&s.a_full[as]);
