@@ -339,6 +339,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8fp4_pair_kernel(const __g
           }
         }
         tmem_st_wait();
+        // The raw slot's next block arrives by TMA (async proxy): order this warp's
+        // generic reads of it before the release.
+        fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.raw_free[slot]);  // the raw slot may take the block after next
         tc_fence_before_sync();
