@@ -162,6 +162,14 @@ constexpr size_t decode_smem_bytes() {
   return sizeof(arcb::a8w4dec::Smem<BT>) + 1024;
 }
 
+// Decode stream mode: some CTA of the plan has more load stages (two K-groups each) than
+// the weight ring holds.
+bool decode_stream(int G, int S, int num_items, int grid) {
+  const int ng_max = (G + S - 1) / S;
+  const int items_max = S > 1 ? 1 : (num_items + grid - 1) / grid;
+  return items_max * ((ng_max + 1) / 2) > static_cast<int>(arcb::a8w4dec::kWStages);
+}
+
 // The persistent-tile instantiations the dispatcher can pick (M > 32).
 #define ARC_A8W4_VARIANTS(X) \
   X(64, 1, 4)                \
@@ -208,21 +216,23 @@ int init_device(int dev) {
                        "gemm_a8w4_kernel was compiled with an unexpected register count");
       return;
     }
-    if (e == cudaSuccess) {
-      e = allow_smem(arcb::a8w4dec::gemm_a8w4_decode_kernel<16>, decode_smem_bytes<16>());
-    }
-    if (e == cudaSuccess) {
-      e = allow_smem(arcb::a8w4dec::gemm_a8w4_decode_kernel<32>, decode_smem_bytes<32>());
-    }
-    // The decode kernels move registers between warpgroups as well (64 per thread at
-    // launch, two CTAs per SM).
-    for (int v = 0; v < 2 && e == cudaSuccess; ++v) {
-      cudaFuncAttributes fa;
-      e = v == 0 ? cudaFuncGetAttributes(&fa, arcb::a8w4dec::gemm_a8w4_decode_kernel<16>)
-                 : cudaFuncGetAttributes(&fa, arcb::a8w4dec::gemm_a8w4_decode_kernel<32>);
-      if (e == cudaSuccess && fa.numRegs != static_cast<int>(arcb::a8w4dec::kLaunchRegs)) {
-        st.status = fail(ARC_ERR_UNSUPPORTED, "gemm_a8w4_decode_kernel was compiled with an unexpected register count");
-        return;
+    // The decode kernels (token tile x chunk / stream mode) also move registers between
+    // warpgroups (64 per thread at launch, two CTAs per SM).
+    {
+      namespace D = arcb::a8w4dec;
+      const void* kerns[4] = {reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<16, false>),
+                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<16, true>),
+                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<32, false>),
+                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<32, true>)};
+      for (int v = 0; v < 4 && e == cudaSuccess; ++v) {
+        const size_t smem = v < 2 ? decode_smem_bytes<16>() : decode_smem_bytes<32>();
+        e = cudaFuncSetAttribute(kerns[v], cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        cudaFuncAttributes fa;
+        if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, kerns[v]);
+        if (e == cudaSuccess && fa.numRegs != static_cast<int>(D::kLaunchRegs)) {
+          st.status = fail(ARC_ERR_UNSUPPORTED, "gemm_a8w4_decode_kernel was compiled with an unexpected register count");
+          return;
+        }
       }
     }
     if (e == cudaSuccess) {
@@ -270,7 +280,7 @@ int init_device(int dev) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, arcb::a8w4dec::gemm_a8w4_decode_kernel<32>, &cfg) !=
+      if (cudaOccupancyMaxActiveClusters(&n, arcb::a8w4dec::gemm_a8w4_decode_kernel<32, false>, &cfg) !=
           cudaSuccess) {
         cudaGetLastError();  // clear; plans then avoid clusters of this size
         n = 0;
@@ -597,7 +607,10 @@ int arc_kernel_name(int op, int M, int N, int K, char* name, int len) {
     arc_a8w4_plan_t plan;
     plan_a8w4(M, N, K, g_dev[dev].sms, g_dev[dev].max_clusters2, g_dev[dev].max_clusters4, &plan);
     if (M <= static_cast<int>(kDecodeMaxM)) {
-      kernel = plan.token_tile == 16 ? "gemm_a8w4_decode_kernel<16>" : "gemm_a8w4_decode_kernel<32>";
+      const bool str = decode_stream(K / static_cast<int>(arcb::a8w4::kGroupK), plan.k_split,
+                                     ceil_div(N, static_cast<int>(arcb::a8w4::kRows)), plan.grid);
+      kernel = plan.token_tile == 16 ? (str ? "gemm_a8w4_decode_kernel<16,true>" : "gemm_a8w4_decode_kernel<16,false>")
+                                     : (str ? "gemm_a8w4_decode_kernel<32,true>" : "gemm_a8w4_decode_kernel<32,false>");
     } else {
       kernel = plan.token_tile == 64 ? "gemm_a8w4_kernel<64,1,4>" : "gemm_a8w4_kernel<128,2,3>";
     }
@@ -1012,14 +1025,14 @@ int a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_
     p.static_weights = (flags & ARC_A8W4_STATIC_WEIGHTS) ? 1u : 0u;
     p.sb_vec = (G % 8 == 0 && aligned16(sb)) ? 1u : 0u;
     const uint32_t grid = static_cast<uint32_t>(plan.grid);
-    // Stream mode when some CTA has more load stages than the ring holds.
-    const uint32_t ng_max = ceil_div(G, S);
-    const uint32_t items_max = S > 1 ? 1u : ceil_div(p.num_items, grid);
-    p.stream = items_max * ((ng_max + 1) / 2) > D::kWStages ? 1u : 0u;
+    const bool str = decode_stream(static_cast<int>(G), static_cast<int>(S), static_cast<int>(p.num_items),
+                                   static_cast<int>(grid));
     if (BT == 16) {
-      e = launch_ex(D::gemm_a8w4_decode_kernel<16>, p, grid, D::kThreads, decode_smem_bytes<16>(), S, stream);
+      e = str ? launch_ex(D::gemm_a8w4_decode_kernel<16, true>, p, grid, D::kThreads, decode_smem_bytes<16>(), S, stream)
+              : launch_ex(D::gemm_a8w4_decode_kernel<16, false>, p, grid, D::kThreads, decode_smem_bytes<16>(), S, stream);
     } else {
-      e = launch_ex(D::gemm_a8w4_decode_kernel<32>, p, grid, D::kThreads, decode_smem_bytes<32>(), S, stream);
+      e = str ? launch_ex(D::gemm_a8w4_decode_kernel<32, true>, p, grid, D::kThreads, decode_smem_bytes<32>(), S, stream)
+              : launch_ex(D::gemm_a8w4_decode_kernel<32, false>, p, grid, D::kThreads, decode_smem_bytes<32>(), S, stream);
     }
     if (e != cudaSuccess) return cuda_fail(e, "gemm_a8w4_decode_kernel launch");
     return ARC_OK;

@@ -82,11 +82,6 @@ struct Params {
   uint32_t split;      // Wp in the pre-packed layout (a8w4::expand_piece)
   uint32_t static_weights;  // Wp and sb are not written by the preceding kernel
   uint32_t sb_vec;     // sb rows 16-byte aligned with G % 8 == 0: 8 scales per load
-  // Stream mode, for CTAs with more load stages than the ring holds: both groups of a
-  // stage are unpacked into TMEM (two stage slots of 64 columns), so a ring stage is free
-  // as soon as it has been read and the loads run ahead of the UMMAs. Otherwise (chunk
-  // mode) the second group stays in the ring stage, unpacked in place, until its UMMAs.
-  uint32_t stream;
   // Fused all-gather (peers > 0): every output tile is stored into each rank's output
   // through tm_peer[i], the [M][N] column window of rank i's gathered [M][world*N] output
   // that this rank owns (peer memory over NVLink; TMA stores only). tm_out is then unused.
@@ -112,6 +107,13 @@ struct Cfg {
   static constexpr uint32_t kDBase = kWStages * 32;
   static constexpr uint32_t kDStages = BT == 16 ? 4 : 2;
   static_assert(kDBase + kDStages * 2 * BT <= kTmemCols, "TMEM budget");
+  // Stream mode: kStreamA weight slots of one stage (both groups, 64 columns) first, then
+  // kStreamD accumulator slots. Three weight slots let a stage's unpack wait for the
+  // UMMAs of the stage three back rather than two (BT=16; BT=32 has room for two).
+  static constexpr uint32_t kStreamA = BT == 16 ? 3 : 2;
+  static constexpr uint32_t kStreamDBase = kStreamA * 64;
+  static constexpr uint32_t kStreamD = 2;
+  static_assert(kStreamDBase + kStreamD * 2 * BT <= kTmemCols, "TMEM budget (stream mode)");
 };
 
 template <uint32_t BT>
@@ -125,7 +127,7 @@ struct alignas(1024) Smem {
   uint64_t w_full[kWStages];
   uint64_t w_empty[kWStages];                   // the stage's UMMAs retired
   uint64_t a_full[kWStages];                    // the stage is unpacked
-  uint64_t a_empty[2];                          // stream mode: a TMEM stage slot's UMMAs retired
+  uint64_t a_empty[C::kStreamA];                // stream mode: a TMEM stage slot's UMMAs retired
   uint64_t t_full[C::kTStages];
   uint64_t t_empty[C::kTStages];
   uint64_t mma_done[C::kDStages];               // a stage's UMMAs retired
@@ -222,7 +224,12 @@ __device__ __forceinline__ float window_scale(const uint4& w, uint32_t j) {
   return __uint_as_float((j & 1u) ? (word & 0xFFFF0000u) : (word << 16));
 }
 
-template <uint32_t BT>
+// STREAM: stream mode, for CTAs with more load stages than the ring holds: both groups
+// of a stage are unpacked into TMEM (Cfg::kStreamA stage slots of 64 columns), so a ring
+// stage is free as soon as it has been read and the loads run ahead of the UMMAs.
+// Otherwise (chunk mode) the second group stays in the ring stage, unpacked in place,
+// until its UMMAs. The host picks the instantiation; each compiles only its own mode.
+template <uint32_t BT, bool STREAM>
 __global__ void __launch_bounds__(kThreads, 2)
     gemm_a8w4_decode_kernel(const __grid_constant__ Params p) {
   using C = Cfg<BT>;
@@ -250,10 +257,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (uint32_t i = lane; i < kWStages; i += 32) {
       mbar_init(&s.w_full[i], 1);
       // Freed by the stage's issuer (chunk mode) or by the four unpack warps (stream mode).
-      mbar_init(&s.w_empty[i], p.stream ? 4 : 1);
+      mbar_init(&s.w_empty[i], STREAM ? 4 : 1);
       mbar_init(&s.a_full[i], 4);   // the four warps of the stage's unpack warpgroup
     }
-    for (uint32_t i = lane; i < 2; i += 32) mbar_init(&s.a_empty[i], 1);
+    for (uint32_t i = lane; i < C::kStreamA; i += 32) mbar_init(&s.a_empty[i], 1);
     for (uint32_t i = lane; i < C::kTStages; i += 32) {
       mbar_init(&s.t_full[i], 1);
       mbar_init(&s.t_empty[i], 1);
@@ -287,6 +294,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t tmem_base = s.tmem_base;
   const Walk wk(p);
   const uint32_t ns = wk.stages();
+  // Accumulator slots of the mode: a power of two, stage t uses slot t & dmask.
+  const uint32_t dsh = STREAM ? 1u : (C::kDStages == 4 ? 2u : 1u);
+  const uint32_t dmask = (1u << dsh) - 1u;
+  const uint32_t dbase = STREAM ? C::kStreamDBase : C::kDBase;
 
   // Register moves sit inside each role's branch, so that the compiler gives every
   // role's code the budget of that role.
@@ -361,25 +372,25 @@ __global__ void __launch_bounds__(kThreads, 2)
       uint32_t ck = 0, cj = 0;  // (tile, stage) of stage t
       wk.advance(ck, cj, q);
       for (uint32_t t = q; ok && t < ns; t += 2, wk.advance(ck, cj, 2)) {
-        const uint32_t ts = t % C::kTStages, ws = t % kWStages, ds = t % C::kDStages;
+        const uint32_t ts = t % C::kTStages, ws = t % kWStages, ds = t & dmask;
         // A slot of the stage: the ring slot (chunk mode) or one of two TMEM stage slots.
-        const uint32_t as = p.stream ? (t & 1u) : ws;
-        const uint32_t a_par = p.stream ? ((t >> 1) & 1u) : ((t / kWStages) & 1u);
+        const uint32_t as = STREAM ? (t % C::kStreamA) : ws;
+        const uint32_t a_par = STREAM ? ((t / C::kStreamA) & 1u) : ((t / kWStages) & 1u);
         // The three tests are issued together (each costs ~200 cycles even when complete).
         const uint32_t t_t = mbar_test(&s.t_full[ts], (t / C::kTStages) & 1u);
         const uint32_t t_a = mbar_test(&s.a_full[as], a_par);
-        const uint32_t t_d = t < C::kDStages ? 1u : mbar_test(&s.tmem_empty[ds], ((t / C::kDStages) & 1u) ^ 1u);
+        const uint32_t t_d = t <= dmask ? 1u : mbar_test(&s.tmem_empty[ds], ((t >> dsh) & 1u) ^ 1u);
         if ((t_t == 0u && !mbar_wait_poll(&s.t_full[ts], (t / C::kTStages) & 1u, abort, kStatusTimeoutMma)) ||
             (t_a == 0u && !mbar_wait_poll(&s.a_full[as], a_par, abort, kStatusTimeoutMma)) ||
             (t_d == 0u &&
-             !mbar_wait_poll(&s.tmem_empty[ds], ((t / C::kDStages) & 1u) ^ 1u, abort, kStatusTimeoutMma))) {
+             !mbar_wait_poll(&s.tmem_empty[ds], ((t >> dsh) & 1u) ^ 1u, abort, kStatusTimeoutMma))) {
           ok = false;
           break;
         }
         tc_fence_after_sync();
         stamp(s, 24 + (t & 7u));  // stage's waits passed
-        const uint32_t d = tmem_base + C::kDBase + ds * 2u * BT;
-        const uint32_t a = tmem_base + as * (p.stream ? 64u : 32u);
+        const uint32_t d = tmem_base + dbase + ds * 2u * BT;
+        const uint32_t a = tmem_base + as * (STREAM ? 64u : 32u);
         const uint64_t b = desc_advance(tdesc0, ts * C::kTokStage);
         // The two groups' K steps alternate, so consecutive UMMAs accumulate into
         // different TMEM columns and the tensor pipe never waits on the previous one.
@@ -390,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (uint32_t j = 0; j < 4; ++j) {
           umma_s8_tmem_a(d, a + 8u * j, desc_advance(b, 32 * j), idesc, j > 0 ? 1u : 0u);
           if (two) {
-            if (p.stream) {
+            if (STREAM) {
               umma_s8_tmem_a(d + BT, a + 32u + 8u * j, desc_advance(b2, 32 * j), idesc, j > 0 ? 1u : 0u);
             } else {
               umma_s8(d + BT, desc_advance(w, 32 * j), desc_advance(b2, 32 * j), idesc, j > 0 ? 1u : 0u);
@@ -398,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
         }
         umma_commit(&s.mma_done[ds]);
-        umma_commit(p.stream ? &s.a_empty[as] : &s.w_empty[ws]);
+        umma_commit(STREAM ? &s.a_empty[as] : &s.w_empty[ws]);
         umma_commit(&s.t_empty[ts]);
         stamp(s, 16 + (t & 15u));  // stage issued
       }
@@ -420,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // With static weights the stages that fit the A slots are unpacked before the
     // preceding grid is waited for; every later wait depends on the UMMAs, hence on the
     // tokens.
-    const uint32_t pre = p.stream ? 2u : kWStages;
+    const uint32_t pre = STREAM ? C::kStreamA : kWStages;
     bool waited = !p.static_weights;
     if (waited) pdl_wait();
     uint32_t uk = 0, uj = 0;  // (tile, stage) of stage t
@@ -431,13 +442,14 @@ __global__ void __launch_bounds__(kThreads, 2)
         waited = true;
       }
       const uint32_t ws = t % kWStages;
-      const uint32_t as = p.stream ? (t & 1u) : ws;
+      const uint32_t as = STREAM ? (t % C::kStreamA) : ws;
       if (!warp_wait(&s.w_full[ws], (t / kWStages) & 1u, abort, kStatusTimeoutUnpack) ||
-          (p.stream && t >= 2 && !warp_wait(&s.a_empty[as], ((t >> 1) & 1u) ^ 1u, abort, kStatusTimeoutUnpack))) {
+          (STREAM && t >= C::kStreamA &&
+           !warp_wait(&s.a_empty[as], ((t / C::kStreamA) & 1u) ^ 1u, abort, kStatusTimeoutUnpack))) {
         ok = false;
         break;
       }
-      if (p.stream) tc_fence_after_sync();  // the TMEM slot's previous UMMAs have retired
+      if (STREAM) tc_fence_after_sync();  // the TMEM slot's previous UMMAs have retired
       uint8_t* row = s.wring[ws] + nl * (kGps * kPackedRow);
       uint4 x[8];
 #pragma unroll
@@ -458,10 +470,10 @@ __global__ void __launch_bounds__(kThreads, 2)
           v[8 * c + 6] = hi.z;
           v[8 * c + 7] = hi.w;
         }
-        tmem_st_32x32b_x16(tmem_base + lane_addr + as * (p.stream ? 64u : 32u) + 16u * h, v);
+        tmem_st_32x32b_x16(tmem_base + lane_addr + as * (STREAM ? 64u : 32u) + 16u * h, v);
       }
       if (wk.has_second(uj)) {
-        if (p.stream) {
+        if (STREAM) {
           // Second group: TMEM columns [64 * slot + 32, +32).
 #pragma unroll
           for (uint32_t h = 0; h < 2; ++h) {
@@ -497,11 +509,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc_fence_before_sync();
       // Stream mode frees the ring stage for a TMA reload (async proxy): order this
       // warp's generic reads of it first.
-      if (p.stream) fence_proxy_async_smem();
+      if (STREAM) fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&s.a_full[as]);
-        if (p.stream) mbar_arrive(&s.w_empty[ws]);  // the stage has been read: reload it
+        if (STREAM) mbar_arrive(&s.w_empty[ws]);  // the stage has been read: reload it
       }
       if ((warp & 7u) == 4u && lane == 0 && t + 2 >= (ns < pre ? ns : pre) && t < pre) stamp(s, 4);  // pre-wait stages unpacked
     }
@@ -559,11 +571,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         win_cur = win_nxt;
         win_nxt = load_window(gi / 8u + 1u);
       }
-      const uint32_t ds = t % C::kDStages;
-      if (ok) ok = warp_wait_poll(&s.mma_done[ds], (t / C::kDStages) & 1u, abort, kStatusTimeoutEpilogue);
+      const uint32_t ds = t & dmask;
+      if (ok) ok = warp_wait_poll(&s.mma_done[ds], (t >> dsh) & 1u, abort, kStatusTimeoutEpilogue);
       if (ok) {
         tc_fence_after_sync();
-        const uint32_t dcol = tmem_base + lane_addr + C::kDBase + ds * 2u * BT;
+        const uint32_t dcol = tmem_base + lane_addr + dbase + ds * 2u * BT;
         // 1/16 undoes the high-nibble placement of the weights.
         const float s0 = window_scale(win_cur, gi & 7u) * 0.0625f;
         const float s1 = second ? window_scale(win_cur, (gi + 1u) & 7u) * 0.0625f : 0.f;
