@@ -220,12 +220,16 @@ int init_device(int dev) {
     // warpgroups (64 per thread at launch, two CTAs per SM).
     {
       namespace D = arcb::a8w4dec;
-      const void* kerns[4] = {reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<16, false>),
-                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<16, true>),
-                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<32, false>),
-                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<32, true>)};
-      for (int v = 0; v < 4 && e == cudaSuccess; ++v) {
-        const size_t smem = v < 2 ? decode_smem_bytes<16>() : decode_smem_bytes<32>();
+      const void* kerns[8] = {reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<16, false, false>),
+                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<16, true, false>),
+                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<16, false, true>),
+                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<16, true, true>),
+                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<32, false, false>),
+                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<32, true, false>),
+                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<32, false, true>),
+                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<32, true, true>)};
+      for (int v = 0; v < 8 && e == cudaSuccess; ++v) {
+        const size_t smem = v < 4 ? decode_smem_bytes<16>() : decode_smem_bytes<32>();
         e = cudaFuncSetAttribute(kerns[v], cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         cudaFuncAttributes fa;
         if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, kerns[v]);
@@ -280,7 +284,7 @@ int init_device(int dev) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, arcb::a8w4dec::gemm_a8w4_decode_kernel<32, false>, &cfg) !=
+      if (cudaOccupancyMaxActiveClusters(&n, arcb::a8w4dec::gemm_a8w4_decode_kernel<32, false, false>, &cfg) !=
           cudaSuccess) {
         cudaGetLastError();  // clear; plans then avoid clusters of this size
         n = 0;
@@ -447,6 +451,17 @@ cudaError_t launch_ex(Kern kernel, const P& p, uint32_t grid, uint32_t threads, 
   return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
+// Launch the decode instantiation of the mode (stream or chunk) and of the partials dump.
+template <uint32_t BT>
+cudaError_t launch_decode(const arcb::a8w4dec::Params& p, uint32_t grid, uint32_t S, bool str, bool dump,
+                          cudaStream_t stream) {
+  namespace D = arcb::a8w4dec;
+  auto k = str ? (dump ? D::gemm_a8w4_decode_kernel<BT, true, true> : D::gemm_a8w4_decode_kernel<BT, true, false>)
+               : (dump ? D::gemm_a8w4_decode_kernel<BT, false, true> : D::gemm_a8w4_decode_kernel<BT, false, false>);
+  return launch_ex(k, p, grid, D::kThreads, decode_smem_bytes<BT>(), S, stream);
+}
+
+
 // bf16 kernel choice. CTA pairs (256 x 256 tiles, half the shared-memory traffic per
 // MAC) once the pair tiles give every co-resident pair one; one CTA per 128 x 256 tile
 // below that (e.g. 2048^3: 64 pair tiles would leave 20 SMs idle, 128 one-CTA tiles
@@ -609,8 +624,9 @@ int arc_kernel_name(int op, int M, int N, int K, char* name, int len) {
     if (M <= static_cast<int>(kDecodeMaxM)) {
       const bool str = decode_stream(K / static_cast<int>(arcb::a8w4::kGroupK), plan.k_split,
                                      ceil_div(N, static_cast<int>(arcb::a8w4::kRows)), plan.grid);
-      kernel = plan.token_tile == 16 ? (str ? "gemm_a8w4_decode_kernel<16,true>" : "gemm_a8w4_decode_kernel<16,false>")
-                                     : (str ? "gemm_a8w4_decode_kernel<32,true>" : "gemm_a8w4_decode_kernel<32,false>");
+      kernel = plan.token_tile == 16
+                   ? (str ? "gemm_a8w4_decode_kernel<16,true,false>" : "gemm_a8w4_decode_kernel<16,false,false>")
+                   : (str ? "gemm_a8w4_decode_kernel<32,true,false>" : "gemm_a8w4_decode_kernel<32,false,false>");
     } else {
       kernel = plan.token_tile == 64 ? "gemm_a8w4_kernel<64,1,4>" : "gemm_a8w4_kernel<128,2,3>";
     }
@@ -1027,13 +1043,8 @@ int a8w4_gemm(const int8_t* A, const float* sa, const uint8_t* Wp, const uint16_
     const uint32_t grid = static_cast<uint32_t>(plan.grid);
     const bool str = decode_stream(static_cast<int>(G), static_cast<int>(S), static_cast<int>(p.num_items),
                                    static_cast<int>(grid));
-    if (BT == 16) {
-      e = str ? launch_ex(D::gemm_a8w4_decode_kernel<16, true>, p, grid, D::kThreads, decode_smem_bytes<16>(), S, stream)
-              : launch_ex(D::gemm_a8w4_decode_kernel<16, false>, p, grid, D::kThreads, decode_smem_bytes<16>(), S, stream);
-    } else {
-      e = str ? launch_ex(D::gemm_a8w4_decode_kernel<32, true>, p, grid, D::kThreads, decode_smem_bytes<32>(), S, stream)
-              : launch_ex(D::gemm_a8w4_decode_kernel<32, false>, p, grid, D::kThreads, decode_smem_bytes<32>(), S, stream);
-    }
+    const bool dump = partials_dbg != nullptr;
+    e = BT == 16 ? launch_decode<16>(p, grid, S, str, dump, stream) : launch_decode<32>(p, grid, S, str, dump, stream);
     if (e != cudaSuccess) return cuda_fail(e, "gemm_a8w4_decode_kernel launch");
     return ARC_OK;
   }

@@ -228,8 +228,9 @@ __device__ __forceinline__ float window_scale(const uint4& w, uint32_t j) {
 // of a stage are unpacked into TMEM (Cfg::kStreamA stage slots of 64 columns), so a ring
 // stage is free as soon as it has been read and the loads run ahead of the UMMAs.
 // Otherwise (chunk mode) the second group stays in the ring stage, unpacked in place,
-// until its UMMAs. The host picks the instantiation; each compiles only its own mode.
-template <uint32_t BT, bool STREAM>
+// until its UMMAs. DUMP: write the exact int32 group partials (a debugging aid) to
+// p.partials. The host picks the instantiation; each compiles only its own code.
+template <uint32_t BT, bool STREAM, bool DUMP>
 __global__ void __launch_bounds__(kThreads, 2)
     gemm_a8w4_decode_kernel(const __grid_constant__ Params p) {
   using C = Cfg<BT>;
@@ -590,7 +591,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (second) accumulate<16>(acc, r, 16, s1);
         } else {
           accumulate<32>(acc, r, 0, s0);
-          if (p.partials != nullptr && n_valid) {
+          if (DUMP && n_valid) {
             const uint32_t g = wk.g0 + gi;
 #pragma unroll
             for (uint32_t c = 0; c < 32; ++c) {
@@ -606,7 +607,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (lane == 0) mbar_arrive(&s.tmem_empty[ds]);
           if (second) accumulate<32>(acc, r, 0, s1);
         }
-        if (p.partials != nullptr && n_valid) {
+        if (DUMP && n_valid) {
           // r holds the second group's partials (BT=32), or both groups' (BT=16).
           const uint32_t g = wk.g0 + gi;
 #pragma unroll
