@@ -162,6 +162,18 @@ constexpr size_t decode_smem_bytes() {
   return sizeof(arcb::a8w4dec::Smem<BT>) + 1024;
 }
 
+// The decode instantiations the dispatcher can launch: token tile x stream mode x K split,
+// each plain, with the partials dump, or with the fused all-gather.
+#define ARC_DECODE_VARIANTS_MODE(X, BT, STR, SK) \
+  X(BT, STR, false, SK, false)                   \
+  X(BT, STR, true, SK, false)                    \
+  X(BT, STR, false, SK, true)
+#define ARC_DECODE_VARIANTS_BT(X, BT)                                            \
+  ARC_DECODE_VARIANTS_MODE(X, BT, false, false) ARC_DECODE_VARIANTS_MODE(X, BT, false, true) \
+  ARC_DECODE_VARIANTS_MODE(X, BT, true, false) ARC_DECODE_VARIANTS_MODE(X, BT, true, true)
+#define ARC_DECODE_VARIANTS(X) ARC_DECODE_VARIANTS_BT(X, 16) ARC_DECODE_VARIANTS_BT(X, 32)
+constexpr int kDecodeVariants = 24;
+
 // Decode stream mode: some CTA of the plan has more load stages (two K-groups each) than
 // the weight ring holds.
 bool decode_stream(int G, int S, int num_items, int grid) {
@@ -220,16 +232,16 @@ int init_device(int dev) {
     // warpgroups (64 per thread at launch, two CTAs per SM).
     {
       namespace D = arcb::a8w4dec;
-      const void* kerns[8] = {reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<16, false, false>),
-                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<16, true, false>),
-                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<16, false, true>),
-                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<16, true, true>),
-                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<32, false, false>),
-                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<32, true, false>),
-                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<32, false, true>),
-                              reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<32, true, true>)};
-      for (int v = 0; v < 8 && e == cudaSuccess; ++v) {
-        const size_t smem = v < 4 ? decode_smem_bytes<16>() : decode_smem_bytes<32>();
+      const void* kerns[kDecodeVariants];
+      size_t smems[kDecodeVariants];
+      int nk = 0;
+#define ARC_DECODE_KERN(BT, STR, DUMP, SK, GATHER)                                        \
+  kerns[nk] = reinterpret_cast<const void*>(D::gemm_a8w4_decode_kernel<BT, STR, DUMP, SK, GATHER>); \
+  smems[nk++] = decode_smem_bytes<BT>();
+      ARC_DECODE_VARIANTS(ARC_DECODE_KERN)
+#undef ARC_DECODE_KERN
+      for (int v = 0; v < nk && e == cudaSuccess; ++v) {
+        const size_t smem = smems[v];
         e = cudaFuncSetAttribute(kerns[v], cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         cudaFuncAttributes fa;
         if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, kerns[v]);
@@ -284,7 +296,7 @@ int init_device(int dev) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, arcb::a8w4dec::gemm_a8w4_decode_kernel<32, false, false>, &cfg) !=
+      if (cudaOccupancyMaxActiveClusters(&n, arcb::a8w4dec::gemm_a8w4_decode_kernel<32, false, false, true, false>, &cfg) !=
           cudaSuccess) {
         cudaGetLastError();  // clear; plans then avoid clusters of this size
         n = 0;
@@ -452,13 +464,25 @@ cudaError_t launch_ex(Kern kernel, const P& p, uint32_t grid, uint32_t threads, 
 }
 
 // Launch the decode instantiation of the mode (stream or chunk) and of the partials dump.
+template <uint32_t BT, bool STR, bool SK>
+cudaError_t launch_decode_mode(const arcb::a8w4dec::Params& p, uint32_t grid, uint32_t S, bool dump, bool gather,
+                               cudaStream_t stream) {
+  namespace D = arcb::a8w4dec;
+  auto k = gather ? D::gemm_a8w4_decode_kernel<BT, STR, false, SK, true>
+                  : (dump ? D::gemm_a8w4_decode_kernel<BT, STR, true, SK, false>
+                          : D::gemm_a8w4_decode_kernel<BT, STR, false, SK, false>);
+  return launch_ex(k, p, grid, D::kThreads, decode_smem_bytes<BT>(), S, stream);
+}
 template <uint32_t BT>
 cudaError_t launch_decode(const arcb::a8w4dec::Params& p, uint32_t grid, uint32_t S, bool str, bool dump,
                           cudaStream_t stream) {
-  namespace D = arcb::a8w4dec;
-  auto k = str ? (dump ? D::gemm_a8w4_decode_kernel<BT, true, true> : D::gemm_a8w4_decode_kernel<BT, true, false>)
-               : (dump ? D::gemm_a8w4_decode_kernel<BT, false, true> : D::gemm_a8w4_decode_kernel<BT, false, false>);
-  return launch_ex(k, p, grid, D::kThreads, decode_smem_bytes<BT>(), S, stream);
+  const bool gather = p.peers > 0;
+  if (str) {
+    return S > 1 ? launch_decode_mode<BT, true, true>(p, grid, S, dump, gather, stream)
+                 : launch_decode_mode<BT, true, false>(p, grid, S, dump, gather, stream);
+  }
+  return S > 1 ? launch_decode_mode<BT, false, true>(p, grid, S, dump, gather, stream)
+               : launch_decode_mode<BT, false, false>(p, grid, S, dump, gather, stream);
 }
 
 
@@ -624,9 +648,12 @@ int arc_kernel_name(int op, int M, int N, int K, char* name, int len) {
     if (M <= static_cast<int>(kDecodeMaxM)) {
       const bool str = decode_stream(K / static_cast<int>(arcb::a8w4::kGroupK), plan.k_split,
                                      ceil_div(N, static_cast<int>(arcb::a8w4::kRows)), plan.grid);
-      kernel = plan.token_tile == 16
-                   ? (str ? "gemm_a8w4_decode_kernel<16,true,false>" : "gemm_a8w4_decode_kernel<16,false,false>")
-                   : (str ? "gemm_a8w4_decode_kernel<32,true,false>" : "gemm_a8w4_decode_kernel<32,false,false>");
+      static const char* kNames[2][2][2] = {
+          {{"gemm_a8w4_decode_kernel<16,false,false,false,false>", "gemm_a8w4_decode_kernel<16,false,false,true,false>"},
+           {"gemm_a8w4_decode_kernel<16,true,false,false,false>", "gemm_a8w4_decode_kernel<16,true,false,true,false>"}},
+          {{"gemm_a8w4_decode_kernel<32,false,false,false,false>", "gemm_a8w4_decode_kernel<32,false,false,true,false>"},
+           {"gemm_a8w4_decode_kernel<32,true,false,false,false>", "gemm_a8w4_decode_kernel<32,true,false,true,false>"}}};
+      kernel = kNames[plan.token_tile == 16 ? 0 : 1][str ? 1 : 0][plan.k_split > 1 ? 1 : 0];
     } else {
       kernel = plan.token_tile == 64 ? "gemm_a8w4_kernel<64,1,4>" : "gemm_a8w4_kernel<128,2,3>";
     }

@@ -163,8 +163,9 @@ __device__ __forceinline__ void stamp(Smem<BT>& s, uint32_t slot) {
 // (a tile with an odd group count ends with a one-group stage), flattened.
 struct Walk {
   uint32_t g0, ng, spi, items;
-  __device__ __forceinline__ explicit Walk(const Params& p) {
-    if (p.S > 1) {
+  bool sk;  // K split over the cluster (S > 1)
+  __device__ __forceinline__ Walk(const Params& p, bool k_split) : sk(k_split) {
+    if (sk) {
       const uint32_t r = blockIdx.x % p.S;
       g0 = r * p.G / p.S;
       ng = (r + 1) * p.G / p.S - g0;
@@ -178,7 +179,7 @@ struct Walk {
   }
   __device__ __forceinline__ uint32_t stages() const { return items * spi; }
   __device__ __forceinline__ uint32_t n0(const Params& p, uint32_t k) const {
-    return (p.S > 1 ? blockIdx.x / p.S : blockIdx.x + k * gridDim.x) * kRows;
+    return (sk ? blockIdx.x / p.S : blockIdx.x + k * gridDim.x) * kRows;
   }
   // Stage t covers groups 2j and 2j + 1 (if 2j + 1 < ng) of tile k, with k = t / spi and
   // j = t % spi. Loops keep (k, j) as a cursor and step it, instead of dividing.
@@ -229,8 +230,9 @@ __device__ __forceinline__ float window_scale(const uint4& w, uint32_t j) {
 // stage is free as soon as it has been read and the loads run ahead of the UMMAs.
 // Otherwise (chunk mode) the second group stays in the ring stage, unpacked in place,
 // until its UMMAs. DUMP: write the exact int32 group partials (a debugging aid) to
-// p.partials. The host picks the instantiation; each compiles only its own code.
-template <uint32_t BT, bool STREAM, bool DUMP>
+// p.partials. SK: K split over the cluster (p.S > 1). GATHER: fused all-gather
+// (p.peers > 0). The host picks the instantiation; each compiles only its own code.
+template <uint32_t BT, bool STREAM, bool DUMP, bool SK, bool GATHER>
 __global__ void __launch_bounds__(kThreads, 2)
     gemm_a8w4_decode_kernel(const __grid_constant__ Params p) {
   using C = Cfg<BT>;
@@ -277,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     fence_barrier_init();
     __syncwarp();
-    if (lane == 0 && p.S > 1) {
+    if (lane == 0 && SK) {
       // Armed before the cluster barrier below, so every peer's bulk copy lands on a
       // barrier that already expects it.
       mbar_arrive_expect_tx(&s.recv_full, (p.S - 1) * (kRows / p.S) * BT * 4u);
@@ -290,10 +292,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
-  if (p.S > 1) cluster_sync_all();  // every CTA's barriers exist before any exchange
+  if (SK) cluster_sync_all();  // every CTA's barriers exist before any exchange
   if (threadIdx.x == 0) stamp(s, 1);  // prologue done
   const uint32_t tmem_base = s.tmem_base;
-  const Walk wk(p);
+  const Walk wk(p, SK);
   const uint32_t ns = wk.stages();
   // Accumulator slots of the mode: a power of two, stage t uses slot t & dmask.
   const uint32_t dsh = STREAM ? 1u : (C::kDStages == 4 ? 2u : 1u);
@@ -627,7 +629,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
       // ---------------------------------------------------------- tile complete
       const uint32_t n0 = wk.n0(p, k);
-      if (p.S == 1) {
+      if constexpr (!SK) {
         // Whole K range here: scale by sa, stage the [BT][128] bf16 tile, one TMA store.
         uint16_t* tile = reinterpret_cast<uint16_t*>(s.recv);  // recv is unused when S == 1
         if (et == 0) tma_store_wait_read<0>();  // the previous tile's store has read it
@@ -640,7 +642,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         fence_proxy_async_smem();
         named_barrier_sync(1, 128);
         if (et == 0 && *abort == 0u) {
-          if (p.peers == 0) {
+          if (!GATHER) {
             tma_store_2d(&p.tm_out, tile, int32_t(n0), 0);
           } else {
             for (uint32_t i = 0; i < p.peers; ++i) tma_store_2d(&p.tm_peer[i], tile, int32_t(n0), 0);
@@ -689,7 +691,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         named_barrier_sync(1, 128);
         if (et == 0) stamp(s, 9);  // tile complete
         if (et == 0 && *abort == 0u) {
-          if (p.peers == 0) {
+          if (!GATHER) {
             tma_store_2d(&p.tm_out, tile, int32_t(n0 + rank * rows_per), 0);
           } else {
             for (uint32_t i = 0; i < p.peers; ++i) {
@@ -704,13 +706,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     // The stores must have read their shared-memory tile before the CTA exits; their
     // global writes complete with the grid.
     if (et == 0) {
-      if (p.bar_world > 0) {
+      if (GATHER && p.bar_world > 0) {
         tma_store_wait_all<0>();  // every store (into every rank's output) performed
       } else {
         tma_store_wait_read<0>();
       }
     }
-    if (p.bar_world > 0 && qw == 0) {
+    if (GATHER && p.bar_world > 0 && qw == 0) {
       // Folded barrier: the CTA that completes the count announces this rank's next epoch
       // in every rank's flags and waits for every rank's (bounded), as peer_barrier.cuh
       // does in a launch of its own.
@@ -753,7 +755,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     regs_release<kRegsCtl>();  // warp 2 (TMEM allocator) shares the producer's warpgroup
   }
 
-  if (p.S > 1) {
+  if (SK) {
     // No CTA leaves while a peer's bulk copy may still read its shared memory (or write
     // into it): every thread arrives when its role is done, the epilogue threads after
     // their recv_full wait. The copies' data is ordered by the transaction counts, so
