@@ -648,11 +648,12 @@ int arc_kernel_name(int op, int M, int N, int K, char* name, int len) {
     if (M <= static_cast<int>(kDecodeMaxM)) {
       const bool str = decode_stream(K / static_cast<int>(arcb::a8w4::kGroupK), plan.k_split,
                                      ceil_div(N, static_cast<int>(arcb::a8w4::kRows)), plan.grid);
+      // As ncu lists them: gemm_a8w4_decode_kernel<BT, STREAM, DUMP, SK, GATHER>.
       static const char* kNames[2][2][2] = {
-          {{"gemm_a8w4_decode_kernel<16,false,false,false,false>", "gemm_a8w4_decode_kernel<16,false,false,true,false>"},
-           {"gemm_a8w4_decode_kernel<16,true,false,false,false>", "gemm_a8w4_decode_kernel<16,true,false,true,false>"}},
-          {{"gemm_a8w4_decode_kernel<32,false,false,false,false>", "gemm_a8w4_decode_kernel<32,false,false,true,false>"},
-           {"gemm_a8w4_decode_kernel<32,true,false,false,false>", "gemm_a8w4_decode_kernel<32,true,false,true,false>"}}};
+          {{"gemm_a8w4_decode_kernel<16, 0, 0, 0, 0>", "gemm_a8w4_decode_kernel<16, 0, 0, 1, 0>"},
+           {"gemm_a8w4_decode_kernel<16, 1, 0, 0, 0>", "gemm_a8w4_decode_kernel<16, 1, 0, 1, 0>"}},
+          {{"gemm_a8w4_decode_kernel<32, 0, 0, 0, 0>", "gemm_a8w4_decode_kernel<32, 0, 0, 1, 0>"},
+           {"gemm_a8w4_decode_kernel<32, 1, 0, 0, 0>", "gemm_a8w4_decode_kernel<32, 1, 0, 1, 0>"}}};
       kernel = kNames[plan.token_tile == 16 ? 0 : 1][str ? 1 : 0][plan.k_split > 1 ? 1 : 0];
     } else {
       kernel = plan.token_tile == 64 ? "gemm_a8w4_kernel<64,1,4>" : "gemm_a8w4_kernel<128,2,3>";
