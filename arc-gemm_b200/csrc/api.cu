@@ -464,6 +464,8 @@ cudaError_t launch_ex(Kern kernel, const P& p, uint32_t grid, uint32_t threads, 
 }
 
 // Launch the decode instantiation of the mode (stream or chunk) and of the partials dump.
+// The fused-gather entry points pass no partials buffer, so the gather instantiations
+// carry no dump.
 template <uint32_t BT, bool STR, bool SK>
 cudaError_t launch_decode_mode(const arcb::a8w4dec::Params& p, uint32_t grid, uint32_t S, bool dump, bool gather,
                                cudaStream_t stream) {
