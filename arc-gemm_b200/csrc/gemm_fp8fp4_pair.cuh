@@ -71,7 +71,7 @@ constexpr uint32_t kSfaBytes = kTileT * kBlk * 4;      // fp32 per token row and
 // Register shares per warpgroup (setmaxnreg): producer / issuer / allocator warps and the
 // converters drop to kRegsCtl / kRegsConv, the epilogue (128 packed columns) rises to
 // kRegsHigh, out of kLaunchRegs per thread at launch.
-constexpr uint32_t kRegsCtl = 96, kRegsConv = 96, kRegsHigh = 160, kLaunchRegs = 128;
+constexpr uint32_t kRegsCtl = 72, kRegsConv = 120, kRegsHigh = 160, kLaunchRegs = 128;
 static_assert(kSfCol + 2 * kSfSlot <= kTmemCols, "accumulator and scale ring fit in TMEM");
 static_assert(128 * kRegsCtl + 128 * kRegsConv + 256 * kRegsHigh <= kThreads * kLaunchRegs, "register shares");
 
