@@ -162,17 +162,18 @@ constexpr size_t decode_smem_bytes() {
   return sizeof(arcb::a8w4dec::Smem<BT>) + 1024;
 }
 
-// The decode instantiations the dispatcher can launch: token tile x stream mode x K split,
+// The decode instantiations the dispatcher can launch: token tile x stream mode x cluster size,
 // each plain, with the partials dump, or with the fused all-gather.
 #define ARC_DECODE_VARIANTS_MODE(X, BT, STR, SK) \
   X(BT, STR, false, SK, false)                   \
   X(BT, STR, true, SK, false)                    \
   X(BT, STR, false, SK, true)
-#define ARC_DECODE_VARIANTS_BT(X, BT)                                            \
-  ARC_DECODE_VARIANTS_MODE(X, BT, false, false) ARC_DECODE_VARIANTS_MODE(X, BT, false, true) \
-  ARC_DECODE_VARIANTS_MODE(X, BT, true, false) ARC_DECODE_VARIANTS_MODE(X, BT, true, true)
+#define ARC_DECODE_VARIANTS_BT(X, BT)                                                            \
+  ARC_DECODE_VARIANTS_MODE(X, BT, false, 1) ARC_DECODE_VARIANTS_MODE(X, BT, false, 2)              \
+  ARC_DECODE_VARIANTS_MODE(X, BT, false, 4) ARC_DECODE_VARIANTS_MODE(X, BT, true, 1)               \
+  ARC_DECODE_VARIANTS_MODE(X, BT, true, 2) ARC_DECODE_VARIANTS_MODE(X, BT, true, 4)
 #define ARC_DECODE_VARIANTS(X) ARC_DECODE_VARIANTS_BT(X, 16) ARC_DECODE_VARIANTS_BT(X, 32)
-constexpr int kDecodeVariants = 24;
+constexpr int kDecodeVariants = 36;
 
 // Decode stream mode: some CTA of the plan has more load stages (two K-groups each) than
 // the weight ring holds.
@@ -296,7 +297,7 @@ int init_device(int dev) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, arcb::a8w4dec::gemm_a8w4_decode_kernel<32, false, false, true, false>, &cfg) !=
+      if (cudaOccupancyMaxActiveClusters(&n, arcb::a8w4dec::gemm_a8w4_decode_kernel<32, false, false, 4, false>, &cfg) !=
           cudaSuccess) {
         cudaGetLastError();  // clear; plans then avoid clusters of this size
         n = 0;
@@ -466,7 +467,7 @@ cudaError_t launch_ex(Kern kernel, const P& p, uint32_t grid, uint32_t threads, 
 // Launch the decode instantiation of the mode (stream or chunk) and of the partials dump.
 // The fused-gather entry points pass no partials buffer, so the gather instantiations
 // carry no dump.
-template <uint32_t BT, bool STR, bool SK>
+template <uint32_t BT, bool STR, uint32_t SK>
 cudaError_t launch_decode_mode(const arcb::a8w4dec::Params& p, uint32_t grid, uint32_t S, bool dump, bool gather,
                                cudaStream_t stream) {
   namespace D = arcb::a8w4dec;
@@ -480,11 +481,13 @@ cudaError_t launch_decode(const arcb::a8w4dec::Params& p, uint32_t grid, uint32_
                           cudaStream_t stream) {
   const bool gather = p.peers > 0;
   if (str) {
-    return S > 1 ? launch_decode_mode<BT, true, true>(p, grid, S, dump, gather, stream)
-                 : launch_decode_mode<BT, true, false>(p, grid, S, dump, gather, stream);
+    return S == 4 ? launch_decode_mode<BT, true, 4>(p, grid, S, dump, gather, stream)
+         : S == 2 ? launch_decode_mode<BT, true, 2>(p, grid, S, dump, gather, stream)
+                  : launch_decode_mode<BT, true, 1>(p, grid, S, dump, gather, stream);
   }
-  return S > 1 ? launch_decode_mode<BT, false, true>(p, grid, S, dump, gather, stream)
-               : launch_decode_mode<BT, false, false>(p, grid, S, dump, gather, stream);
+  return S == 4 ? launch_decode_mode<BT, false, 4>(p, grid, S, dump, gather, stream)
+       : S == 2 ? launch_decode_mode<BT, false, 2>(p, grid, S, dump, gather, stream)
+                : launch_decode_mode<BT, false, 1>(p, grid, S, dump, gather, stream);
 }
 
 
@@ -650,13 +653,17 @@ int arc_kernel_name(int op, int M, int N, int K, char* name, int len) {
     if (M <= static_cast<int>(kDecodeMaxM)) {
       const bool str = decode_stream(K / static_cast<int>(arcb::a8w4::kGroupK), plan.k_split,
                                      ceil_div(N, static_cast<int>(arcb::a8w4::kRows)), plan.grid);
-      // As ncu lists them: gemm_a8w4_decode_kernel<BT, STREAM, DUMP, SK, GATHER>.
-      static const char* kNames[2][2][2] = {
-          {{"gemm_a8w4_decode_kernel<16, 0, 0, 0, 0>", "gemm_a8w4_decode_kernel<16, 0, 0, 1, 0>"},
-           {"gemm_a8w4_decode_kernel<16, 1, 0, 0, 0>", "gemm_a8w4_decode_kernel<16, 1, 0, 1, 0>"}},
-          {{"gemm_a8w4_decode_kernel<32, 0, 0, 0, 0>", "gemm_a8w4_decode_kernel<32, 0, 0, 1, 0>"},
-           {"gemm_a8w4_decode_kernel<32, 1, 0, 0, 0>", "gemm_a8w4_decode_kernel<32, 1, 0, 1, 0>"}}};
-      kernel = kNames[plan.token_tile == 16 ? 0 : 1][str ? 1 : 0][plan.k_split > 1 ? 1 : 0];
+      // As ncu lists them: gemm_a8w4_decode_kernel<BT, STREAM, DUMP, cluster size, GATHER>.
+      static const char* kNames[2][2][3] = {
+          {{"gemm_a8w4_decode_kernel<16, 0, 0, 1, 0>", "gemm_a8w4_decode_kernel<16, 0, 0, 2, 0>",
+            "gemm_a8w4_decode_kernel<16, 0, 0, 4, 0>"},
+           {"gemm_a8w4_decode_kernel<16, 1, 0, 1, 0>", "gemm_a8w4_decode_kernel<16, 1, 0, 2, 0>",
+            "gemm_a8w4_decode_kernel<16, 1, 0, 4, 0>"}},
+          {{"gemm_a8w4_decode_kernel<32, 0, 0, 1, 0>", "gemm_a8w4_decode_kernel<32, 0, 0, 2, 0>",
+            "gemm_a8w4_decode_kernel<32, 0, 0, 4, 0>"},
+           {"gemm_a8w4_decode_kernel<32, 1, 0, 1, 0>", "gemm_a8w4_decode_kernel<32, 1, 0, 2, 0>",
+            "gemm_a8w4_decode_kernel<32, 1, 0, 4, 0>"}}};
+      kernel = kNames[plan.token_tile == 16 ? 0 : 1][str ? 1 : 0][plan.k_split == 4 ? 2 : plan.k_split == 2 ? 1 : 0];
     } else {
       kernel = plan.token_tile == 64 ? "gemm_a8w4_kernel<64,1,4>" : "gemm_a8w4_kernel<128,2,3>";
     }

@@ -163,12 +163,12 @@ __device__ __forceinline__ void stamp(Smem<BT>& s, uint32_t slot) {
 // (a tile with an odd group count ends with a one-group stage), flattened.
 struct Walk {
   uint32_t g0, ng, spi, items;
-  bool sk;  // K split over the cluster (S > 1)
-  __device__ __forceinline__ Walk(const Params& p, bool k_split) : sk(k_split) {
-    if (sk) {
-      const uint32_t r = blockIdx.x % p.S;
-      g0 = r * p.G / p.S;
-      ng = (r + 1) * p.G / p.S - g0;
+  uint32_t S;  // CTAs of the cluster along K (1: persistent tiles, no split)
+  __device__ __forceinline__ Walk(const Params& p, uint32_t cluster) : S(cluster) {
+    if (S > 1) {
+      const uint32_t r = blockIdx.x % S;
+      g0 = r * p.G / S;
+      ng = (r + 1) * p.G / S - g0;
       items = 1;
     } else {
       g0 = 0;
@@ -179,7 +179,7 @@ struct Walk {
   }
   __device__ __forceinline__ uint32_t stages() const { return items * spi; }
   __device__ __forceinline__ uint32_t n0(const Params& p, uint32_t k) const {
-    return (sk ? blockIdx.x / p.S : blockIdx.x + k * gridDim.x) * kRows;
+    return (S > 1 ? blockIdx.x / S : blockIdx.x + k * gridDim.x) * kRows;
   }
   // Stage t covers groups 2j and 2j + 1 (if 2j + 1 < ng) of tile k, with k = t / spi and
   // j = t % spi. Loops keep (k, j) as a cursor and step it, instead of dividing.
@@ -230,9 +230,10 @@ __device__ __forceinline__ float window_scale(const uint4& w, uint32_t j) {
 // stage is free as soon as it has been read and the loads run ahead of the UMMAs.
 // Otherwise (chunk mode) the second group stays in the ring stage, unpacked in place,
 // until its UMMAs. DUMP: write the exact int32 group partials (a debugging aid) to
-// p.partials. SK: K split over the cluster (p.S > 1). GATHER: fused all-gather
-// (p.peers > 0). The host picks the instantiation; each compiles only its own code.
-template <uint32_t BT, bool STREAM, bool DUMP, bool SK, bool GATHER>
+// p.partials. SK: CTAs of the cluster along K (p.S: 1, 2 or 4). GATHER: fused
+// all-gather (p.peers > 0). The host picks the instantiation; each compiles only its own
+// code.
+template <uint32_t BT, bool STREAM, bool DUMP, uint32_t SK, bool GATHER>
 __global__ void __launch_bounds__(kThreads, 2)
     gemm_a8w4_decode_kernel(const __grid_constant__ Params p) {
   using C = Cfg<BT>;
@@ -279,10 +280,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     fence_barrier_init();
     __syncwarp();
-    if (lane == 0 && SK) {
+    if (lane == 0 && SK > 1) {
       // Armed before the cluster barrier below, so every peer's bulk copy lands on a
       // barrier that already expects it.
-      mbar_arrive_expect_tx(&s.recv_full, (p.S - 1) * (kRows / p.S) * BT * 4u);
+      mbar_arrive_expect_tx(&s.recv_full, (SK - 1) * (kRows / SK) * BT * 4u);
     }
   }
   if (warp == 2) {
@@ -292,7 +293,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
-  if (SK) cluster_sync_all();  // every CTA's barriers exist before any exchange
+  if (SK > 1) cluster_sync_all();  // every CTA's barriers exist before any exchange
   if (threadIdx.x == 0) stamp(s, 1);  // prologue done
   const uint32_t tmem_base = s.tmem_base;
   const Walk wk(p, SK);
@@ -629,7 +630,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
       // ---------------------------------------------------------- tile complete
       const uint32_t n0 = wk.n0(p, k);
-      if constexpr (!SK) {
+      if constexpr (SK == 1) {
         // Whole K range here: scale by sa, stage the [BT][128] bf16 tile, one TMA store.
         uint16_t* tile = reinterpret_cast<uint16_t*>(s.recv);  // recv is unused when S == 1
         if (et == 0) tma_store_wait_read<0>();  // the previous tile's store has read it
@@ -655,8 +656,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         // ring, the peers' slices are shipped as one bulk copy per peer into
         // recv[this rank], then all 128 threads sum the owned slice in rank order and
         // one TMA store writes it.
-        const uint32_t rank = blockIdx.x % p.S;
-        const uint32_t rows_per = kRows / p.S;
+        const uint32_t rank = blockIdx.x % SK;
+        constexpr uint32_t rows_per = kRows / (SK > 1 ? SK : 1);
         float* send = reinterpret_cast<float*>(s.wring);
         uint16_t* tile = reinterpret_cast<uint16_t*>(&s.wring[0][0] + kRows * BT * 4u);
         float4* dst = reinterpret_cast<float4*>(send + nl * BT);
@@ -666,7 +667,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         named_barrier_sync(1, 128);
         if (et == 0 && *abort == 0u) {
           stamp(s, 5);  // partials staged
-          for (uint32_t o = 0; o < p.S; ++o) {
+          for (uint32_t o = 0; o < SK; ++o) {
             if (o == rank) continue;
             bulk_copy_to_peer(map_to_rank(s.recv + rank * rows_per * BT, o), send + o * rows_per * BT,
                               rows_per * BT * 4u, map_to_rank(&s.recv_full, o));
@@ -680,7 +681,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (uint32_t e = et; e < rows_per * BT; e += 128) {
             const uint32_t rr = e / BT, c = e % BT;  // c == et % BT: sa_mine is its scale
             float sum = 0.f;
-            for (uint32_t src = 0; src < p.S; ++src) {  // fixed order: deterministic
+            for (uint32_t src = 0; src < SK; ++src) {  // fixed order: deterministic
               sum += src == rank ? own[e] : s.recv[src * rows_per * BT + e];
             }
             tile[c * rows_per + rr] = __bfloat16_as_ushort(__float2bfloat16_rn(sum * sa_mine));
@@ -755,7 +756,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     regs_release<kRegsCtl>();  // warp 2 (TMEM allocator) shares the producer's warpgroup
   }
 
-  if (SK) {
+  if (SK > 1) {
     // No CTA leaves while a peer's bulk copy may still read its shared memory (or write
     // into it): every thread arrives when its role is done, the epilogue threads after
     // their recv_full wait. The copies' data is ordered by the transaction counts, so

@@ -99,9 +99,9 @@ def test_kernel_name_matches_the_shape_rules(cuda_device):
     from arc import _lib
     assert arc.kernel_name(_lib.OP_MATMUL_BF16, 8192, 8192, 8192) == "gemm_bf16_pair_kernel"
     assert arc.kernel_name(_lib.OP_MATMUL_BF16, 128, 256, 64) == "gemm_bf16_kernel"
-    # decode instantiations: <token tile, stream mode, partials dump, K split, fused gather>
-    assert arc.kernel_name(_lib.OP_A8W4, 16, 4096, 4096) == "gemm_a8w4_decode_kernel<16, 0, 0, 1, 0>"
-    assert arc.kernel_name(_lib.OP_A8W4, 16, 28672, 8192) == "gemm_a8w4_decode_kernel<16, 1, 0, 0, 0>"
+    # decode instantiations: <token tile, stream mode, partials dump, cluster size, fused gather>
+    assert arc.kernel_name(_lib.OP_A8W4, 16, 4096, 4096) == "gemm_a8w4_decode_kernel<16, 0, 0, 4, 0>"
+    assert arc.kernel_name(_lib.OP_A8W4, 16, 28672, 8192) == "gemm_a8w4_decode_kernel<16, 1, 0, 1, 0>"
     assert arc.kernel_name(_lib.OP_A8W4, 4096, 14336, 4096) == "gemm_a8w4_kernel<128,2,3>"
     assert arc.kernel_name(_lib.OP_FP8_FP4, 4096, 14336, 4096) == "gemm_fp8fp4_pair_kernel"
     assert arc.kernel_name(_lib.OP_FP8_FP4, 16, 4096, 4096) == "gemm_fp8fp4_kernel<1>"
