@@ -529,6 +529,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t nl = qw * 32 + lane;             // row of the tile = TMEM lane
     const uint32_t lane_addr = (qw * 32u) << 16;
     bool ok = true;
+    bool cl_arrived = false;  // arrived at the end-of-kernel cluster barrier (S > 1)
 
     // Weight scales of this row for the current tile, 8 K-groups per window: the
     // current window and the next one are in registers.
@@ -674,6 +675,11 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
         }
         const bool got = warp_wait_poll(&s.recv_full, 0, abort, kStatusTimeoutEpilogue);
+        // Every copy into this CTA has landed: arriving now lets the end-of-kernel
+        // cluster barrier complete while the slice is summed and stored.
+        __syncwarp();
+        cluster_arrive_relaxed();
+        cl_arrived = true;
         if (et == 0) stamp(s, 6);  // peer partials landed
         if (got) {
           const float sa_mine = __shfl_sync(0xffffffffu, sa_lane, lane % BT);  // token et % BT
@@ -703,6 +709,10 @@ __global__ void __launch_bounds__(kThreads, 2)
           stamp(s, 7);  // output store issued
         }
       }
+    }
+    if (SK > 1 && !cl_arrived) {  // no tile completed here (not reached with a valid plan)
+      __syncwarp();
+      cluster_arrive_relaxed();
     }
     // The stores must have read their shared-memory tile before the CTA exits; their
     // global writes complete with the grid.
@@ -762,7 +772,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // their recv_full wait. The copies' data is ordered by the transaction counts, so
     // the arrival orders nothing (relaxed).
     __syncwarp();
-    cluster_arrive_relaxed();
+    if (warp < 8 || warp >= 12) cluster_arrive_relaxed();  // the epilogue warps have arrived
     cluster_wait();
     if (threadIdx.x == 0) stamp(s, 14);  // end-of-kernel cluster barrier passed
   }
