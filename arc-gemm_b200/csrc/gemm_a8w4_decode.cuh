@@ -56,11 +56,16 @@ using a8w4::kRows;
 
 constexpr uint32_t kThreads = 512;
 constexpr uint32_t kLaunchRegs = 64;  // 2 CTAs per SM
-constexpr uint32_t kRegsCtl = 40, kRegsUnpack = 64;
+constexpr uint32_t kRegsUnpack = 64;
+// The control warpgroup's share (producer, UMMA issuers, TMEM allocator: one lane each
+// works); BT = 32 hands 8 of its registers on to the epilogue.
+template <uint32_t BT>
+__host__ __device__ constexpr uint32_t regs_ctl() { return BT == 16 ? 40u : 32u; }
 // The epilogue's share: its BT running sums plus one stage's 32 partials and the scales.
 template <uint32_t BT>
-__host__ __device__ constexpr uint32_t regs_epi() { return BT == 16 ? 80u : 88u; }
-static_assert(128 * (kRegsCtl + 2 * kRegsUnpack + regs_epi<32>()) <= kThreads * kLaunchRegs, "register shares");
+__host__ __device__ constexpr uint32_t regs_epi() { return BT == 16 ? 80u : 96u; }
+static_assert(128 * (regs_ctl<16>() + 2 * kRegsUnpack + regs_epi<16>()) <= kThreads * kLaunchRegs, "register shares");
+static_assert(128 * (regs_ctl<32>() + 2 * kRegsUnpack + regs_epi<32>()) <= kThreads * kLaunchRegs, "register shares");
 constexpr uint32_t kTmemCols = 256;   // half an SM's TMEM: two CTAs share one SM
 constexpr uint32_t kGps = 2;          // K-groups per load stage (one 128-byte box row)
 constexpr uint32_t kWStageBytes = kRows * kGps * kPackedRow;  // 16 KiB of packed weights
@@ -307,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   // role's code the budget of that role.
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    regs_release<kRegsCtl>();
+    regs_release<regs_ctl<BT>()>();
     // Weight stages run up to kWStages ahead of token stages; with static weights the
     // first kWStages are issued before the wait for the preceding grid.
     if (lane == 0) {
@@ -358,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   } else if (warp == 1 || warp == 3) {
     // ------------------------------------------------------------ UMMA issuers
-    regs_release<kRegsCtl>();
+    regs_release<regs_ctl<BT>()>();
     // Issuer q takes the stages t with t % 2 == q. A stage: four K=32 UMMAs of its first
     // group (A from TMEM) and four of its second (A from the unpacked shared-memory
     // stage), B from the stage's token tiles, into the accumulator pair of slot
@@ -413,8 +418,10 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
         }
         umma_commit(&s.mma_done[ds]);
-        umma_commit(STREAM ? &s.a_empty[as] : &s.w_empty[ws]);
-        umma_commit(&s.t_empty[ts]);
+        // The slot-release commits only where a later stage reloads the slot (each
+        // tcgen05 instruction costs the issuer tens of cycles).
+        if (t + (STREAM ? C::kStreamA : kWStages) < ns) umma_commit(STREAM ? &s.a_empty[as] : &s.w_empty[ws]);
+        if (t + C::kTStages < ns) umma_commit(&s.t_empty[ts]);
         stamp(s, 16 + (t & 15u));  // stage issued
       }
       umma_commit(&s.drain);
@@ -654,9 +661,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       } else {
         // K split over the S-CTA cluster; rank r finishes rows [r*128/S, (r+1)*128/S).
         // Every row's partial is staged as send[row][token] in the (now idle) weight
-        // ring, the peers' slices are shipped as one bulk copy per peer into
-        // recv[this rank], then all 128 threads sum the owned slice in rank order and
-        // one TMA store writes it.
+        // ring. A warp's 32 rows lie in one rank's slice: a warp of a peer's slice ships
+        // its rows with one bulk copy into recv[this rank] of that peer as soon as they
+        // are staged. Then all 128 threads sum the owned slice in rank order and one TMA
+        // store writes it.
         const uint32_t rank = blockIdx.x % SK;
         constexpr uint32_t rows_per = kRows / (SK > 1 ? SK : 1);
         float* send = reinterpret_cast<float*>(s.wring);
@@ -664,22 +672,25 @@ __global__ void __launch_bounds__(kThreads, 2)
         float4* dst = reinterpret_cast<float4*>(send + nl * BT);
 #pragma unroll
         for (uint32_t c = 0; c < BT; c += 4) dst[c / 4] = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
-        fence_proxy_async_smem();
-        named_barrier_sync(1, 128);
-        if (et == 0 && *abort == 0u) {
-          stamp(s, 5);  // partials staged
-          for (uint32_t o = 0; o < SK; ++o) {
-            if (o == rank) continue;
-            bulk_copy_to_peer(map_to_rank(s.recv + rank * rows_per * BT, o), send + o * rows_per * BT,
-                              rows_per * BT * 4u, map_to_rank(&s.recv_full, o));
+        const uint32_t owner = qw * 32u / rows_per;  // rank whose slice holds this warp's rows
+        if (owner != rank) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && *abort == 0u) {
+            // rows qw*32.. are rows (qw*32) % rows_per.. of the owner's slice
+            bulk_copy_to_peer(map_to_rank(s.recv + (rank * rows_per + (qw * 32u) % rows_per) * BT, owner),
+                              reinterpret_cast<const float*>(dst) - lane * BT, 32u * BT * 4u,
+                              map_to_rank(&s.recv_full, owner));
           }
         }
+        if (et == 0) stamp(s, 5);  // partials staged
         const bool got = warp_wait_poll(&s.recv_full, 0, abort, kStatusTimeoutEpilogue);
         // Every copy into this CTA has landed: arriving now lets the end-of-kernel
         // cluster barrier complete while the slice is summed and stored.
         __syncwarp();
         cluster_arrive_relaxed();
         cl_arrived = true;
+        named_barrier_sync(1, 128);  // the owned rows staged by other warps are visible
         if (et == 0) stamp(s, 6);  // peer partials landed
         if (got) {
           const float sa_mine = __shfl_sync(0xffffffffu, sa_lane, lane % BT);  // token et % BT
@@ -763,7 +774,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
   } else {
-    regs_release<kRegsCtl>();  // warp 2 (TMEM allocator) shares the producer's warpgroup
+    regs_release<regs_ctl<BT>()>();  // warp 2 (TMEM allocator) shares the producer's warpgroup
   }
 
   if (SK > 1) {
