@@ -608,7 +608,7 @@ class Runner:
         kname = rec["roofline"]["kernel"]
         if self.gather == "fused" and kname.startswith("gemm_a8w4_decode_kernel<") and kname.endswith(", 0>"):
             # the last template argument of the decode kernel is the fused-gather flag
-            rec["roofline"]["kernel"] = kname[:-3] + "1>"
+            rec["roofline"]["kernel"] = kname[:-2] + "1>"
         if e2e is not None:
             rec["e2e"] = {"value": ops_total / (e2e_ms * 1e-3) / 1e12, "unit": unit,
                           "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
