@@ -178,11 +178,13 @@ def test_a8w4_decode_decompositions(cuda_device, monkeypatch, plan):
     walks several tiles (the A slots, load stages and accumulators carry over between
     tiles). K = 384 and 640 give one-group load stages and uneven splits; K = 8192 and the
     capped grids give CTAs with more load stages than the ring holds (stream mode: both
-    groups of a stage unpacked into TMEM, ring stages refilled ahead of the UMMAs)."""
+    groups of a stage unpacked into TMEM, ring stages refilled ahead of the UMMAs), with 16
+    and with 32 tokens per tile. A second call without the partials buffer runs the
+    production instantiation of the same plan and must give the same output bit for bit."""
     monkeypatch.setenv("ARC_DECODE_PLAN", plan)
     S = int(plan.split(":")[1])
     for m, n, k in ((16, 1000, 1024), (3, 512, 2048), (32, 256, 512), (16, 1000, 384), (7, 264, 640),
-                    (16, 384, 8192)):
+                    (16, 384, 8192), (32, 256, 8192)):
         for static in (False, True):
             (x, sa), (wp, sb) = generate_a8w4(m, n, k, seed=S + m + k)
             dev = cuda_device
@@ -197,6 +199,11 @@ def test_a8w4_decode_decompositions(cuda_device, monkeypatch, plan):
             ref = oracle.a8w4_out(x.numpy(), sa.numpy(), wp.numpy(), _bits(sb))
             ok, msg = oracle.check_bf16_close(out.float().cpu().numpy(), ref, max_ulp=2.0)
             assert ok, f"plan {plan} {m}x{n}x{k} static={static}: {msg}"
+            out2 = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=dev)
+            arc.a8w4_matmul((x.to(dev), sa.to(dev)), (wp.to(dev), sb.to(dev)), out2, static_weights=static)
+            torch.cuda.synchronize()
+            assert arc.device_status(0) == 0, "kernel reported a wait timeout"
+            assert torch.equal(out2, out), f"plan {plan} {m}x{n}x{k} static={static}: no-dump output differs"
 
 
 @pytest.mark.parametrize("m,n,k", [(16, 4096, 4096), (32, 1000, 1024), (1, 28672, 8192)])
